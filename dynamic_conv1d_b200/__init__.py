@@ -1,0 +1,17 @@
+"""B200-native dynamic short convolutions (drop-in for OliverSieberling/dynamic-conv1d).
+
+    from dynamic_conv1d_b200 import headwise_dynamic_convolution, lowrank_dynamic_convolution
+
+Both ops are ``torch.autograd.Function``s over libdynconv.so, a C-ABI library of
+hand-written sm_100a CUDA kernels (see ``include/dynconv.h``).
+"""
+from .headwise import headwise_dynamic_convolution
+from .lowrank import lowrank_dynamic_convolution
+from .parallel import data_parallel, shard_rows
+
+__all__ = [
+    "headwise_dynamic_convolution",
+    "lowrank_dynamic_convolution",
+    "data_parallel",
+    "shard_rows",
+]

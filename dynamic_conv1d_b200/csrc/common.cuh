@@ -1,0 +1,343 @@
+// common.cuh -- shared device/host helpers of libdynconv (sm_100a only).
+//
+// * element access for bf16 / fp32 tensors (16-byte vector loads, RNE stores)
+// * the device error word that bounded waits set when they give up
+// * thin inline-PTX wrappers for mbarrier, TMA (cp.async.bulk.tensor) and the
+//   5th-generation tensor core (tcgen05: TMEM alloc, mma, commit, ld)
+#pragma once
+
+#include <cuda.h>
+#include <cuda_bf16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include "../../include/dynconv.h"
+
+#if defined(__CUDA_ARCH__) && (__CUDA_ARCH__ != 1000)
+#error "libdynconv is written for sm_100a (B200) only"
+#endif
+
+namespace dynconv {
+
+// ----------------------------------------------------------------- host side
+
+// Records `msg` as the calling thread's last error and returns `status`.
+int set_error(int status, const char* fmt, ...);
+// Wraps a CUDA runtime status: DYNCONV_OK or DYNCONV_ERR_CUDA with the CUDA message.
+int cuda_status(cudaError_t e, const char* what);
+// Number of SMs of the current device (cached per device).
+int sm_count();
+
+// Counts kernel launches (dynconv_launch_count) -- call once per launch.
+void note_launch(int n = 1);
+
+#define DYNCONV_CHECK_LAUNCH(what)                                  \
+  do {                                                              \
+    cudaError_t e__ = cudaGetLastError();                           \
+    if (e__ != cudaSuccess) return ::dynconv::cuda_status(e__, what); \
+    ::dynconv::note_launch();                                       \
+  } while (0)
+
+// --------------------------------------------------------------- device side
+
+// Set to a nonzero site code by a bounded wait that gave up.  Without relocatable
+// device code a __device__ variable cannot be shared between translation units,
+// so every .cu file that waits on mbarriers gets its own copy (internal linkage)
+// and exports a host accessor with DYNCONV_DEFINE_ERROR_ACCESSOR, which
+// dynconv_check_device() polls.
+static __device__ unsigned int g_device_error;
+
+#define DYNCONV_DEFINE_ERROR_ACCESSOR(fn)                                      \
+  unsigned int fn() {                                                          \
+    unsigned int v = 0;                                                        \
+    if (cudaMemcpyFromSymbol(&v, g_device_error, sizeof(v)) != cudaSuccess)    \
+      return 0xFFFFFFFFu;                                                      \
+    if (v != 0) {                                                              \
+      const unsigned int z = 0;                                                \
+      cudaMemcpyToSymbol(g_device_error, &z, sizeof(z));                       \
+    }                                                                          \
+    return v;                                                                  \
+  }
+
+enum DeviceErrorSite : unsigned int {
+  kErrNone = 0,
+  kErrWaitProducer = 1,
+  kErrWaitMma = 2,
+  kErrWaitEpilogue = 3,
+  kErrWaitTail = 4,
+};
+
+template <typename T>
+struct Elem;
+
+template <>
+struct Elem<__nv_bfloat16> {
+  static constexpr int kVec = 8;  // elements per 16-byte vector
+  __device__ __forceinline__ static float to_f(__nv_bfloat16 v) { return __bfloat162float(v); }
+  __device__ __forceinline__ static __nv_bfloat16 from_f(float v) { return __float2bfloat16_rn(v); }
+};
+
+template <>
+struct Elem<float> {
+  static constexpr int kVec = 4;
+  __device__ __forceinline__ static float to_f(float v) { return v; }
+  __device__ __forceinline__ static float from_f(float v) { return v; }
+};
+
+// Loads N consecutive elements starting at p into float registers.  When the
+// span is 16-byte aligned (checked at run time; uniform across a warp in all
+// call sites) it is read as 16-byte vectors, otherwise element by element.
+template <typename T, int N>
+__device__ __forceinline__ void load_span(const T* __restrict__ p, float (&out)[N]) {
+  constexpr int kBytes = N * (int)sizeof(T);
+  if (kBytes % 16 == 0 && ((reinterpret_cast<uintptr_t>(p) & 15) == 0)) {
+    constexpr int kV = 16 / (int)sizeof(T);
+#pragma unroll
+    for (int i = 0; i < N; i += kV) {
+      uint4 u = __ldg(reinterpret_cast<const uint4*>(p + i));
+      const T* e = reinterpret_cast<const T*>(&u);
+#pragma unroll
+      for (int j = 0; j < kV; ++j) out[i + j] = Elem<T>::to_f(e[j]);
+    }
+  } else if (kBytes % 8 == 0 && ((reinterpret_cast<uintptr_t>(p) & 7) == 0)) {
+    constexpr int kV = 8 / (int)sizeof(T);
+#pragma unroll
+    for (int i = 0; i < N; i += kV) {
+      uint2 u = __ldg(reinterpret_cast<const uint2*>(p + i));
+      const T* e = reinterpret_cast<const T*>(&u);
+#pragma unroll
+      for (int j = 0; j < kV; ++j) out[i + j] = Elem<T>::to_f(e[j]);
+    }
+  } else {
+#pragma unroll
+    for (int i = 0; i < N; ++i) out[i] = Elem<T>::to_f(p[i]);
+  }
+}
+
+template <typename T, int N>
+__device__ __forceinline__ void store_span(T* __restrict__ p, const float (&v)[N]) {
+  constexpr int kBytes = N * (int)sizeof(T);
+  if (kBytes % 16 == 0 && ((reinterpret_cast<uintptr_t>(p) & 15) == 0)) {
+    constexpr int kV = 16 / (int)sizeof(T);
+#pragma unroll
+    for (int i = 0; i < N; i += kV) {
+      uint4 u;
+      T* e = reinterpret_cast<T*>(&u);
+#pragma unroll
+      for (int j = 0; j < kV; ++j) e[j] = Elem<T>::from_f(v[i + j]);
+      *reinterpret_cast<uint4*>(p + i) = u;
+    }
+  } else if (kBytes % 8 == 0 && ((reinterpret_cast<uintptr_t>(p) & 7) == 0)) {
+    constexpr int kV = 8 / (int)sizeof(T);
+#pragma unroll
+    for (int i = 0; i < N; i += kV) {
+      uint2 u;
+      T* e = reinterpret_cast<T*>(&u);
+#pragma unroll
+      for (int j = 0; j < kV; ++j) e[j] = Elem<T>::from_f(v[i + j]);
+      *reinterpret_cast<uint2*>(p + i) = u;
+    }
+  } else {
+#pragma unroll
+    for (int i = 0; i < N; ++i) p[i] = Elem<T>::from_f(v[i]);
+  }
+}
+
+// ------------------------------------------------------------ PTX wrappers
+
+__device__ __forceinline__ uint32_t smem_u32(const void* p) {
+  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
+__device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count) : "memory");
+}
+
+__device__ __forceinline__ void fence_barrier_init() {
+  asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+}
+
+__device__ __forceinline__ void fence_proxy_async_smem() {
+  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
+  asm volatile("mbarrier.arrive.release.cta.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t* bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.release.cta.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)),
+               "r"(bytes)
+               : "memory");
+}
+
+__device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.acquire.cta.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+
+// Upper bound on polls of one mbarrier phase.  Each try_wait suspends for a
+// hardware-chosen time slice, so this is on the order of seconds; a wait that
+// runs out records `site` in g_device_error and returns false so the kernel
+// can unwind instead of hanging the GPU.
+constexpr uint32_t kMaxPolls = 1u << 26;
+
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, unsigned int site,
+                                          volatile int* abort_flag) {
+  for (uint32_t i = 0; i < kMaxPolls; ++i) {
+    if (mbar_try_wait(bar, parity)) return true;
+    if ((i & 1023u) == 1023u && *abort_flag) return false;
+  }
+  atomicCAS(&g_device_error, 0u, site);
+  *abort_flag = 1;
+  return false;
+}
+
+// TMA tiled 3-D load into shared memory, completion counted on `bar`.
+__device__ __forceinline__ void tma_load_3d(void* smem_dst, const CUtensorMap* map, uint64_t* bar, int c0,
+                                            int c1, int c2, uint64_t policy) {
+  asm volatile(
+      "cp.async.bulk.tensor.3d.shared::cluster.global.tile.mbarrier::complete_tx::bytes.L2::cache_hint"
+      " [%0], [%1, {%3, %4, %5}], [%2], %6;" ::"r"(smem_u32(smem_dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(smem_u32(bar)), "r"(c0), "r"(c1), "r"(c2), "l"(policy)
+      : "memory");
+}
+
+// TMA tiled 3-D store from shared memory (bulk-group completion).
+__device__ __forceinline__ void tma_store_3d(const CUtensorMap* map, const void* smem_src, int c0, int c1,
+                                             int c2, uint64_t policy) {
+  asm volatile(
+      "cp.async.bulk.tensor.3d.global.shared::cta.tile.bulk_group.L2::cache_hint [%0, {%2, %3, %4}], [%1], %5;" ::"l"(
+          reinterpret_cast<uint64_t>(map)),
+      "r"(smem_u32(smem_src)), "r"(c0), "r"(c1), "r"(c2), "l"(policy)
+      : "memory");
+}
+
+__device__ __forceinline__ void bulk_commit_group() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
+
+template <int N>
+__device__ __forceinline__ void bulk_wait_group_read() {
+  asm volatile("cp.async.bulk.wait_group.read %0;" ::"n"(N) : "memory");
+}
+
+template <int N>
+__device__ __forceinline__ void bulk_wait_group() {
+  asm volatile("cp.async.bulk.wait_group %0;" ::"n"(N) : "memory");
+}
+
+__device__ __forceinline__ void prefetch_tensormap(const CUtensorMap* map) {
+  asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");
+}
+
+__device__ __forceinline__ uint64_t policy_evict_first() {
+  uint64_t p;
+  asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(p));
+  return p;
+}
+
+__device__ __forceinline__ uint64_t policy_evict_last() {
+  uint64_t p;
+  asm volatile("createpolicy.fractional.L2::evict_last.b64 %0, 1.0;" : "=l"(p));
+  return p;
+}
+
+// Named barrier over `count` threads (ids 1..15; 0 is __syncthreads).
+__device__ __forceinline__ void named_bar_sync(int id, int count) {
+  asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(count) : "memory");
+}
+
+// ------------------------------------------------------------------ tcgen05
+
+__device__ __forceinline__ void tmem_alloc(uint32_t* dst_smem, uint32_t ncols) {
+  asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(dst_smem)),
+               "r"(ncols)
+               : "memory");
+}
+
+__device__ __forceinline__ void tmem_relinquish() {
+  asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+}
+
+__device__ __forceinline__ void tmem_dealloc(uint32_t taddr, uint32_t ncols) {
+  asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols) : "memory");
+}
+
+__device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+
+// D[tmem] (+)= A[smem desc] * B[smem desc]; kind::f16 (bf16 inputs, fp32 accumulate).
+__device__ __forceinline__ void umma_f16(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_t idesc,
+                                         uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
+// Arrives once on `bar` when every previously issued tcgen05.mma of this thread completes.
+__device__ __forceinline__ void umma_commit(uint64_t* bar) {
+  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
+                   smem_u32(bar))
+               : "memory");
+}
+
+// 32 lanes x 16 consecutive 32-bit columns; lane i of the warp gets row (base lane + i).
+__device__ __forceinline__ void tmem_ld16(uint32_t taddr, float (&v)[16]) {
+  uint32_t r[16];
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x16.b32 "
+      "{%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15}, [%16];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+        "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
+      : "r"(taddr));
+#pragma unroll
+  for (int i = 0; i < 16; ++i) v[i] = __uint_as_float(r[i]);
+}
+
+__device__ __forceinline__ void tmem_ld_wait() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
+
+// Shared-memory matrix descriptor, SWIZZLE_NONE ("interleaved") canonical layout.
+// lbo: byte stride between 8-element core-matrix groups along K;
+// sbo: byte stride between core-matrix groups along M/N.  Both K-major and
+// MN-major operands use this pairing in the no-swizzle mode.
+__device__ __forceinline__ uint64_t make_smem_desc(uint32_t smem_addr, uint32_t lbo, uint32_t sbo) {
+  uint64_t d = 0;
+  d |= (uint64_t)((smem_addr >> 4) & 0x3FFFu);
+  d |= (uint64_t)((lbo >> 4) & 0x3FFFu) << 16;
+  d |= (uint64_t)((sbo >> 4) & 0x3FFFu) << 32;
+  d |= (uint64_t)1 << 46;  // descriptor version for sm_100
+  // base offset 0, lbo mode 0, layout type 0 (SWIZZLE_NONE)
+  return d;
+}
+
+// Instruction descriptor for kind::f16 with bf16 A/B and fp32 D.
+__host__ __device__ constexpr uint32_t make_idesc_bf16(int M, int N, int a_mn_major, int b_mn_major) {
+  return (1u << 4)                          // D format: F32
+         | (1u << 7)                        // A format: BF16
+         | (1u << 10)                       // B format: BF16
+         | ((uint32_t)a_mn_major << 15)     // A major (0 = K, 1 = MN)
+         | ((uint32_t)b_mn_major << 16)     // B major
+         | ((uint32_t)(N >> 3) << 17)       // N / 8
+         | ((uint32_t)(M >> 4) << 24);      // M / 16
+}
+
+// Byte offset of element (mn, k) in a no-swizzle K-major operand.
+__host__ __device__ __forceinline__ uint32_t kmajor_off(int mn, int k, uint32_t sbo, uint32_t lbo) {
+  return (uint32_t)(mn & 7) * 16u + (uint32_t)(mn >> 3) * sbo + (uint32_t)(k & 7) * 2u + (uint32_t)(k >> 3) * lbo;
+}
+
+// Byte offset of element (mn, k) in a no-swizzle MN-major operand.
+__host__ __device__ __forceinline__ uint32_t mnmajor_off(int mn, int k, uint32_t sbo, uint32_t lbo) {
+  return (uint32_t)(mn & 7) * 2u + (uint32_t)(mn >> 3) * sbo + (uint32_t)(k & 7) * 16u + (uint32_t)(k >> 3) * lbo;
+}
+
+}  // namespace dynconv

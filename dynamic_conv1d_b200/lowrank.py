@@ -1,0 +1,136 @@
+"""Low-rank dynamic short convolution -- drop-in for ``lowrank.py`` of
+OliverSieberling/dynamic-conv1d, backed by libdynconv (sm_100a CUDA kernels).
+
+Same public function, same ``torch.autograd.Function`` structure, same argument
+meaning and the same ``assert`` preconditions as the reference
+(``lowrank.py:214-338``).  Differences that a caller can observe only as
+"more general" or "less memory traffic":
+
+* the static filter is folded in as rank R inside the kernels; nothing is
+  padded or concatenated in HBM (the reference builds ``F.pad(z)`` and
+  ``torch.cat([U, static_w])``, lowrank.py:222-226);
+* the returned ``dz`` / ``dU`` are dense tensors of the caller's shapes (the
+  reference returns slices of padded buffers, lowrank.py:295-299);
+* the dU / dstatic_w reduction is deterministic (fixed-order two-pass; the
+  reference uses fp32 atomics, lowrank.py:137).
+"""
+from __future__ import annotations
+
+import torch
+
+from . import _lib
+from .parallel import allreduce_shared_grad, current_group
+
+
+class _LowrankDynamicConvolutionFn(torch.autograd.Function):
+    """Mirrors ``_LowrankDynamicConvolutionFn`` (lowrank.py:214-299)."""
+
+    @staticmethod
+    def forward(ctx, x, z, U, static_w, residual):
+        B, T, D = x.shape
+        R = z.shape[-1]
+        W = U.shape[-1] // D
+        lib = _lib.load()
+        code = _lib.dtype_code(x.dtype)
+        # The kernels compute in x.dtype; parameters of another dtype are cast
+        # for the call and their gradients cast back.
+        z_k = z if z.dtype == x.dtype else z.to(x.dtype)
+        U_k = U if U.dtype == x.dtype else U.to(x.dtype)
+        sw_k = static_w if (static_w is None or static_w.dtype == x.dtype) else static_w.to(x.dtype)
+        y = torch.empty_like(x)
+        _lib.check(
+            lib.dynconv_lr_fwd(
+                _lib.ptr(x), _lib.ptr(z_k), _lib.ptr(U_k), _lib.ptr(sw_k), _lib.ptr(y),
+                B, T, D, R, W, code, int(bool(residual)), _lib.stream_of(x),
+            )
+        )
+        ctx.save_for_backward(x, z_k, U_k, sw_k)
+        ctx.dtypes = (z.dtype, U.dtype, None if static_w is None else static_w.dtype)
+        ctx.residual = bool(residual)
+        ctx.group = current_group()
+        return y
+
+    @staticmethod
+    def backward(ctx, dy):
+        dy = dy.contiguous()
+        x, z, U, static_w = ctx.saved_tensors
+        B, T, D = x.shape
+        R = z.shape[-1]
+        W = U.shape[-1] // D
+        has_static = static_w is not None
+        Rk = R + (1 if has_static else 0)
+        lib = _lib.load()
+        code = _lib.dtype_code(x.dtype)
+        if dy.dtype != x.dtype:
+            dy = dy.to(x.dtype)
+        dx = torch.empty_like(x)
+        dz = torch.empty_like(z)
+        dU_f32 = torch.empty((Rk, W * D), device=x.device, dtype=torch.float32)
+        nbytes = lib.dynconv_lr_bwd_workspace_bytes(B, T, D, R, W, code, int(has_static))
+        ws = torch.empty(max(int(nbytes), 1), device=x.device, dtype=torch.uint8)
+        reduce_first = ctx.group is not None
+        dU = None if reduce_first else torch.empty_like(U)
+        dsw = None if (reduce_first or not has_static) else torch.empty((W, D), device=x.device, dtype=x.dtype)
+        stream = _lib.stream_of(x)
+        _lib.check(
+            lib.dynconv_lr_bwd(
+                _lib.ptr(x), _lib.ptr(z), _lib.ptr(U), _lib.ptr(static_w), _lib.ptr(dy),
+                _lib.ptr(dx), _lib.ptr(dz), _lib.ptr(dU), _lib.ptr(dsw), _lib.ptr(dU_f32),
+                _lib.ptr(ws), ws.numel(),
+                B, T, D, R, W, code, int(ctx.residual), stream,
+            )
+        )
+        if reduce_first:
+            allreduce_shared_grad(dU_f32, ctx.group)
+            dU = torch.empty_like(U)
+            _lib.check(lib.dynconv_cast_f32(_lib.ptr(dU_f32), _lib.ptr(dU), R * W * D, code, stream))
+            if has_static:
+                dsw = torch.empty((W, D), device=x.device, dtype=x.dtype)
+                _lib.check(lib.dynconv_cast_f32(_lib.ptr(dU_f32[R]), _lib.ptr(dsw), W * D, code, stream))
+        z_dt, U_dt, sw_dt = ctx.dtypes
+        if dz.dtype != z_dt:
+            dz = dz.to(z_dt)
+        if dU.dtype != U_dt:
+            dU = dU.to(U_dt)
+        if dsw is not None and dsw.dtype != sw_dt:
+            dsw = dsw.to(sw_dt)
+        return dx, dz, dU, dsw, None
+
+
+def lowrank_dynamic_convolution(
+    x: torch.Tensor,
+    z: torch.Tensor,
+    U: torch.Tensor,
+    static_w: torch.Tensor | None = None,
+    residual: bool = False,
+) -> torch.Tensor:
+    """Low-rank dynamic short convolution, with optional fused static filter.
+
+    The dynamic weights ``z @ U`` are generated on chip (tensor cores for bf16)
+    and never written to HBM.
+
+    Args:
+        x:        [B, T, D] input activations (bfloat16 or float32, CUDA, contiguous).
+        z:        [B, T, R] hidden states after the first projection.
+        U:        [R, W*D] second projection, viewed as (R, W, D).
+        static_w: [W, D] optional static filter, fused as one extra rank, so
+                  R+1 must be a power of two when it is given (R otherwise).
+        residual: add x to the output.
+
+    Returns:
+        y: [B, T, D] with y[b,t,d] = sum_w (sum_r z[b,t,r] U[r,w*D+d] + static_w[w,d]) * x[b,t-w,d]
+        (+ x[b,t,d] if residual).
+
+    Same preconditions as the reference (lowrank.py:328-337).
+    """
+    assert x.is_cuda and x.is_contiguous()
+    assert z.is_cuda and z.is_contiguous()
+    assert U.is_cuda and U.is_contiguous()
+    R = z.shape[-1]
+    R_kernel = R + 1 if static_w is not None else R
+    assert R_kernel & (R_kernel - 1) == 0, "rank R must be a power of 2. If static_w is set R+1 must be a power of 2."
+    if static_w is not None:
+        assert static_w.is_cuda and static_w.is_contiguous()
+        assert static_w.dtype == z.dtype == U.dtype
+        assert static_w.shape == (U.shape[-1] // x.shape[-1], x.shape[-1])
+    return _LowrankDynamicConvolutionFn.apply(x, z, U, static_w, residual)

@@ -1,0 +1,150 @@
+/*
+ * dynconv.h -- C ABI of the B200 (sm_100a) dynamic short convolution library
+ * (libdynconv.so).  Drop-in boundary for the GPU half of the reference project
+ * OliverSieberling/dynamic-conv1d: each entry point replaces one kernel launch
+ * site (or launch group) of the reference's autograd Functions.
+ *
+ * Conventions
+ *   - All tensors are caller-allocated device buffers, dense row-major
+ *     ("contiguous" in PyTorch terms).  The library never allocates or frees them.
+ *   - `dtype` is a dynconv_dtype; every floating tensor of one call shares it,
+ *     except the explicitly float* accumulators.
+ *   - `stream` is a cudaStream_t passed as void* (0 = legacy default stream).
+ *     Calls are asynchronous: no host synchronisation.
+ *   - Return value: DYNCONV_OK (0) or a dynconv_status error code; the message of
+ *     the last failing call on the calling thread is dynconv_last_error().
+ *   - Shapes: x,y,dx,dy [B,T,D]; headwise weight [B,T,H,W]; lowrank z [B,T,R],
+ *     U [R, W*D] (viewed as [R][W][D]); static_w [W,D].  W in 1..8.
+ */
+#ifndef DYNCONV_H_
+#define DYNCONV_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* The library is built with hidden default visibility; everything declared
+ * here is exported. */
+#if defined(__GNUC__)
+#pragma GCC visibility push(default)
+#endif
+
+#define DYNCONV_ABI_VERSION 1
+
+typedef enum dynconv_dtype {
+  DYNCONV_DTYPE_BF16 = 0,
+  DYNCONV_DTYPE_F32 = 1
+} dynconv_dtype;
+
+typedef enum dynconv_status {
+  DYNCONV_OK = 0,
+  DYNCONV_ERR_SHAPE = 1,       /* inconsistent or out-of-range sizes            */
+  DYNCONV_ERR_ALIGN = 2,       /* a pointer is not aligned as the kernel needs  */
+  DYNCONV_ERR_UNSUPPORTED = 3, /* valid for the reference, not for this build   */
+  DYNCONV_ERR_CUDA = 4,        /* a CUDA runtime/driver call failed             */
+  DYNCONV_ERR_TIMEOUT = 5,     /* a bounded device-side wait gave up            */
+  DYNCONV_ERR_WORKSPACE = 6,   /* workspace missing or too small                */
+  DYNCONV_ERR_ARGUMENT = 7     /* null pointer where a tensor is required       */
+} dynconv_status;
+
+/* Library identity and diagnostics. */
+int dynconv_abi_version(void);
+const char* dynconv_status_string(int status);
+const char* dynconv_last_error(void);
+/* Synchronises `stream`, then reads and clears the device error word that
+ * bounded waits inside the tensor-core kernels set when they give up.
+ * Returns DYNCONV_OK, DYNCONV_ERR_TIMEOUT or DYNCONV_ERR_CUDA. */
+int dynconv_check_device(void* stream);
+/* Number of kernels this library has launched in this process (all devices,
+ * all threads).  Diagnostic only; no reference counterpart. */
+uint64_t dynconv_launch_count(void);
+
+/* ---------------------------------------------------------------- headwise */
+
+/* y = sum_w (weight[b,t,d/hs,w] + static_w[w,d]) * x[b,t-w,d]  (+ x if residual)
+ * Replaces the causal_conv1d_fwd_kernel launch in
+ * _HeadwiseDynamicConvolutionFn.forward (headwise.py:220-254; launch :234-248).
+ * static_w may be NULL.  hs = D/H must be a power of two. */
+int dynconv_hw_fwd(const void* x, const void* weight, const void* static_w, void* y,
+                   int64_t B, int64_t T, int64_t D, int64_t H, int64_t W,
+                   int dtype, int residual, void* stream);
+
+/* Workspace for dynconv_hw_bwd (bytes; 0 when static_w is absent). */
+size_t dynconv_hw_bwd_workspace_bytes(int64_t B, int64_t T, int64_t D, int64_t H, int64_t W,
+                                      int dtype, int has_static);
+
+/* Backward of dynconv_hw_fwd for upstream gradient dy.
+ * Replaces the causal_conv1d_bwd_kernel launch and the dstatic cast in
+ * _HeadwiseDynamicConvolutionFn.backward (headwise.py:257-309; launch :283-300).
+ * Writes dx [B,T,D] and dweight [B,T,H,W] (no power-of-two padding of W).
+ * With static_w != NULL: the float32 sum over (b,t) of dy*x_shift is written to
+ * dstatic_w_f32 [W,D] (required) and, when dstatic_w != NULL, also cast to
+ * `dtype` into dstatic_w.  The reduction is deterministic (fixed-order two-pass). */
+int dynconv_hw_bwd(const void* x, const void* weight, const void* static_w, const void* dy,
+                   void* dx, void* dweight, void* dstatic_w, float* dstatic_w_f32,
+                   void* workspace, size_t workspace_bytes,
+                   int64_t B, int64_t T, int64_t D, int64_t H, int64_t W,
+                   int dtype, int residual, void* stream);
+
+/* ----------------------------------------------------------------- lowrank */
+
+/* y = sum_w ((z@U).view(B,T,W,D)[b,t,w,d] + static_w[w,d]) * x[b,t-w,d] (+ x)
+ * Replaces the static-rank fold (F.pad / torch.cat, lowrank.py:222-226) and the
+ * causal_conv1d_fwd_kernel launch (lowrank.py:230-242) of
+ * _LowrankDynamicConvolutionFn.forward.  static_w is folded in on chip as rank R
+ * (R_kernel = R + 1); nothing is padded or concatenated in HBM.  Any R >= 1 with
+ * R_kernel <= 64 is accepted (the reference needs R_kernel a power of two >= 16). */
+int dynconv_lr_fwd(const void* x, const void* z, const void* U, const void* static_w, void* y,
+                   int64_t B, int64_t T, int64_t D, int64_t R, int64_t W,
+                   int dtype, int residual, void* stream);
+
+/* Workspace for dynconv_lr_bwd (bytes). */
+size_t dynconv_lr_bwd_workspace_bytes(int64_t B, int64_t T, int64_t D, int64_t R, int64_t W,
+                                      int dtype, int has_static);
+
+/* Backward of dynconv_lr_fwd.  Replaces the dU/dz and dx kernel launches, the
+ * float32 dU zero-init and the cast/split of _LowrankDynamicConvolutionFn.backward
+ * (lowrank.py:252-299; launches :266-292).
+ * Writes dx [B,T,D], dz [B,T,R] and the float32 accumulator dU_f32 [R_kernel, W*D]
+ * (rows 0..R-1 = dU, row R = dstatic_w when static_w != NULL; required).  When dU
+ * (and dstatic_w) are non-NULL, the accumulator is also cast to `dtype` into
+ * dU [R, W*D] and dstatic_w [W,D].  Pass dU = dstatic_w = NULL to all-reduce
+ * dU_f32 across data-parallel ranks first and cast afterwards with dynconv_cast_f32. */
+int dynconv_lr_bwd(const void* x, const void* z, const void* U, const void* static_w, const void* dy,
+                   void* dx, void* dz, void* dU, void* dstatic_w, float* dU_f32,
+                   void* workspace, size_t workspace_bytes,
+                   int64_t B, int64_t T, int64_t D, int64_t R, int64_t W,
+                   int dtype, int residual, void* stream);
+
+/* dst[i] = (dtype) src[i], i < n, round-to-nearest-even.  Used after the
+ * data-parallel all-reduce of the float32 shared-gradient buffers (replaces
+ * dU_fp32.to(U.dtype), lowrank.py:294, and dstatic_accum.to(...), headwise.py:305). */
+int dynconv_cast_f32(const float* src, void* dst, int64_t n, int dtype, void* stream);
+
+/* ------------------------------------------------------------- diagnostics */
+
+/* One tcgen05.mma (kind::f16, bf16 in, fp32 accumulate) sequence on operands
+ * staged into the canonical no-swizzle shared-memory layouts used by the
+ * lowrank kernels, for the unit tests of descriptor encodings.  No reference
+ * counterpart.  A: logical [M][K] bf16 row-major; B: logical [K][Nb] bf16
+ * row-major (Nb >= N + b_row_offset); D: [M][N] float32 = A @ B[:, off:off+N].
+ * a_major/b_major: 0 = K-major, 1 = MN-major; *_sbo/*_lbo: byte strides of the
+ * staged layout; b_row_offset shifts a K-major B by whole rows (16 B each). */
+int dynconv_umma_selftest(const void* A, const void* B, float* D,
+                          int M, int N, int K, int Nb,
+                          int a_major, int a_sbo, int a_lbo,
+                          int b_major, int b_sbo, int b_lbo, int b_row_offset,
+                          void* stream);
+
+#if defined(__GNUC__)
+#pragma GCC visibility pop
+#endif
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* DYNCONV_H_ */

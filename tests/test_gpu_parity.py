@@ -1,0 +1,227 @@
+"""GPU parity of the CUDA path (through the public autograd API) with the CPU oracle
+and with the reference's own outputs (golden fixtures).
+
+Tolerances:
+  * bf16: relative L2 <= 1e-2 for y and <= 2e-2 for every gradient, against the
+    reference math run in float32 on the same bf16 values (the BASELINE bar);
+    the reference's own test.py TOL (atol 0.4, rtol 0.5) is also applied.
+  * fp32: test.py's TOL (atol 1e-4, rtol 1e-3) elementwise.
+"""
+from __future__ import annotations
+
+import zlib
+
+import numpy as np
+import pytest
+import torch
+
+import oracle
+from conftest import golden_names, load_golden, rel_l2
+from dynamic_conv1d_b200 import headwise_dynamic_convolution, lowrank_dynamic_convolution
+
+pytestmark = pytest.mark.gpu
+
+TOL = {torch.float32: (1e-4, 1e-3), torch.bfloat16: (4e-1, 5e-1)}  # test.py:17
+REL_L2_Y = 1e-2
+REL_L2_GRAD = 2e-2
+
+
+def _np(t: torch.Tensor) -> np.ndarray:
+    return t.detach().float().cpu().numpy()
+
+
+def _check(name, got: torch.Tensor, ref: np.ndarray, dtype, is_grad: bool):
+    g = _np(got)
+    assert g.shape == ref.shape, (name, g.shape, ref.shape)
+    assert np.isfinite(g).all(), name
+    atol, rtol = TOL[dtype]
+    torch.testing.assert_close(torch.from_numpy(g), torch.from_numpy(ref.astype(np.float32)), atol=atol, rtol=rtol,
+                               msg=lambda m: f"{name}: {m}")
+    if dtype == torch.bfloat16:
+        bound = REL_L2_GRAD if is_grad else REL_L2_Y
+        e = rel_l2(g, ref)
+        assert e <= bound, f"{name}: rel-L2 {e:.3e} > {bound}"
+
+
+def _run(kind, arrays, residual, dtype, dev, has_static):
+    x = torch.from_numpy(arrays["x"]).to(dev, dtype).requires_grad_()
+    dy = torch.from_numpy(arrays["dy"]).to(dev, dtype)
+    sw = torch.from_numpy(arrays["static_w"]).to(dev, dtype).requires_grad_() if has_static else None
+    if kind == "headwise":
+        w = torch.from_numpy(arrays["weight"]).to(dev, dtype).requires_grad_()
+        y = headwise_dynamic_convolution(x, w, sw, residual=residual)
+        y.backward(dy)
+        out = {"y": y, "dx": x.grad, "dweight": w.grad}
+    else:
+        z = torch.from_numpy(arrays["z"]).to(dev, dtype).requires_grad_()
+        U = torch.from_numpy(arrays["U"]).to(dev, dtype).requires_grad_()
+        y = lowrank_dynamic_convolution(x, z, U, sw, residual=residual)
+        y.backward(dy)
+        out = {"y": y, "dx": x.grad, "dz": z.grad, "dU": U.grad}
+    if has_static:
+        out["dstatic_w"] = sw.grad
+    torch.cuda.synchronize()
+    return out
+
+
+def _oracle(kind, a, residual):
+    sw = a.get("static_w")
+    if kind == "headwise":
+        y = oracle.headwise_fwd(a["x"], a["weight"], sw, residual)
+        dx, dw, dsw = oracle.headwise_bwd(a["x"], a["weight"], sw, a["dy"], residual)
+        out = {"y": y, "dx": dx, "dweight": dw}
+    else:
+        y = oracle.lowrank_fwd(a["x"], a["z"], a["U"], sw, residual)
+        dx, dz, dU, dsw = oracle.lowrank_bwd(a["x"], a["z"], a["U"], sw, a["dy"], residual)
+        out = {"y": y, "dx": dx, "dz": dz, "dU": dU}
+    if sw is not None:
+        out["dstatic_w"] = dsw
+    return out
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float32])
+@pytest.mark.parametrize("name", golden_names())
+def test_golden_fixture(name, dtype, cuda_device):
+    case = load_golden(name)
+    m = case["meta"]
+    out = _run(m["kind"], case, m["residual"], dtype, cuda_device, m["has_static"])
+    for k, v in out.items():
+        _check(f"{name}/{k}", v, case[k], dtype, is_grad=(k != "y"))
+
+
+# ---- the reference's own correctness sweep (test.py:9-58), against the oracle
+SWEEP_B, SWEEP_T, SWEEP_D = 2, 512, 256  # test.py:15
+
+
+def _sweep_cases():
+    cases = []
+    for dtype in (torch.bfloat16, torch.float32):
+        for residual in (False, True):
+            for W in (2, 4):
+                for hs in (1, 16):
+                    for st in (False, True):
+                        cases.append(("headwise", dtype, residual, W, hs, st))
+                for st in (False, True):
+                    cases.append(("lowrank", dtype, residual, W, 16, st))
+    return cases
+
+
+@pytest.fixture(scope="module")
+def sweep_inputs(cuda_device):
+    g = torch.Generator(device="cuda").manual_seed(0)
+    x = torch.randn(SWEEP_B, SWEEP_T, SWEEP_D, device="cuda", generator=g)
+    dy = torch.randn(SWEEP_B, SWEEP_T, SWEEP_D, device="cuda", generator=g)
+    per_w = {}
+    for W in (2, 4):
+        sw = torch.randn(W, SWEEP_D, device="cuda", generator=g) * 0.1
+        ws = {hs: torch.randn(SWEEP_B, SWEEP_T, SWEEP_D // hs, W, device="cuda", generator=g) * 0.1 for hs in (1, 16)}
+        z = torch.randn(SWEEP_B, SWEEP_T, 16, device="cuda", generator=g) * (0.1 / 16 ** 0.5)
+        U = torch.randn(16, W * SWEEP_D, device="cuda", generator=g)
+        per_w[W] = (sw, ws, z, U)
+    return x, dy, per_w
+
+
+def test_reference_sweep_has_48_configs():
+    assert len(_sweep_cases()) == 48  # test.py:58 "All 48 configs passed"
+
+
+@pytest.mark.parametrize("case", _sweep_cases(), ids=lambda c: "-".join(str(v).replace("torch.", "") for v in c))
+def test_reference_sweep(case, sweep_inputs, cuda_device):
+    kind, dtype, residual, W, hs, st = case
+    x, dy, per_w = sweep_inputs
+    sw, ws, z_full, U_full = per_w[W]
+    # the kernel sees the values cast to dtype; the oracle runs in fp32 on those values
+    arrays = {"x": _np(x.to(dtype)), "dy": _np(dy.to(dtype))}
+    if st:
+        arrays["static_w"] = _np(sw.to(dtype))
+    if kind == "headwise":
+        arrays["weight"] = _np(ws[hs].to(dtype))
+    else:
+        z = z_full[..., :-1] if st else z_full  # test.py:53-54
+        U = U_full[:-1] if st else U_full
+        arrays["z"] = _np(z.contiguous().to(dtype))
+        arrays["U"] = _np(U.contiguous().to(dtype))
+    out = _run(kind, arrays, residual, dtype, cuda_device, st)
+    ref = _oracle(kind, arrays, residual)
+    for k, v in out.items():
+        _check(f"{kind}/{k}", v, ref[k], dtype, is_grad=(k != "y"))
+
+
+# ---- edge cases the reference does not cover (it needs T, D multiples of 128)
+EDGE = [
+    # kind, B, T, D, H-or-R, W, static, residual
+    ("headwise", 1, 1, 64, 64, 4, True, True),
+    ("headwise", 2, 3, 64, 8, 4, True, False),
+    ("headwise", 1, 37, 20, 5, 3, True, True),      # D % 8 != 0, hs = 4 (one channel per thread for bf16)
+    ("headwise", 2, 300, 512, 4, 4, True, True),    # hs = 128 (largest the reference allows)
+    ("headwise", 1, 129, 96, 96, 8, True, True),    # W = 8
+    ("headwise", 3, 257, 72, 9, 5, False, True),    # hs = 8, W = 5, odd T
+    ("headwise", 1, 50, 16, 16, 1, False, False),   # W = 1
+    ("lowrank", 1, 1, 64, 15, 4, True, True),
+    ("lowrank", 2, 3, 64, 16, 2, False, True),
+    ("lowrank", 1, 37, 20, 7, 3, True, True),       # D % 8 != 0
+    ("lowrank", 2, 300, 256, 31, 4, True, True),    # R_kernel = 32, ragged T
+    ("lowrank", 1, 129, 136, 63, 4, True, False),   # R_kernel = 64, D not a multiple of 128
+    ("lowrank", 1, 70, 128, 15, 8, True, True),     # W = 8
+    ("lowrank", 2, 64, 128, 1, 4, False, True),     # R = 1
+]
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float32])
+@pytest.mark.parametrize("case", EDGE, ids=lambda c: "-".join(str(v) for v in c))
+def test_edge_shapes(case, dtype, cuda_device):
+    kind, B, T, D, HR, W, st, residual = case
+    rng = np.random.default_rng(zlib.crc32(repr(case).encode()))
+
+    def rnd(*shape, scale=1.0):
+        return torch.from_numpy((rng.standard_normal(shape) * scale).astype(np.float32)).to(dtype).float().numpy()
+
+    arrays = {"x": rnd(B, T, D), "dy": rnd(B, T, D)}
+    if st:
+        arrays["static_w"] = rnd(W, D, scale=0.3)
+    if kind == "headwise":
+        arrays["weight"] = rnd(B, T, HR, W, scale=0.3)
+    else:
+        arrays["z"] = rnd(B, T, HR, scale=0.3)
+        arrays["U"] = rnd(HR, W * D, scale=1.0 / np.sqrt(HR))
+    if kind == "lowrank":
+        Rk = HR + (1 if st else 0)
+        if Rk & (Rk - 1):
+            pytest.skip("the reference API requires a power-of-two R_kernel")
+    out = _run(kind, arrays, residual, dtype, cuda_device, st)
+    ref = _oracle(kind, arrays, residual)
+    for k, v in out.items():
+        _check(f"{kind}/{k}", v, ref[k], dtype, is_grad=(k != "y"))
+
+
+@pytest.mark.parametrize("kind", ["headwise", "lowrank"])
+def test_backward_is_deterministic(kind, cuda_device):
+    torch.manual_seed(0)
+    B, T, D, W = 2, 1000, 512, 4
+    x = torch.randn(B, T, D, device="cuda", dtype=torch.bfloat16)
+    dy = torch.randn(B, T, D, device="cuda", dtype=torch.bfloat16)
+    sw = (torch.rand(W, D, device="cuda") - 0.5).to(torch.bfloat16)
+    if kind == "headwise":
+        w = torch.randn(B, T, D // 32, W, device="cuda", dtype=torch.bfloat16)
+        args = [x, w, sw]
+        fn = headwise_dynamic_convolution
+    else:
+        z = torch.randn(B, T, 15, device="cuda", dtype=torch.bfloat16)
+        U = torch.randn(15, W * D, device="cuda", dtype=torch.bfloat16) / 4
+        args = [x, z, U, sw]
+        fn = lowrank_dynamic_convolution
+    grads = []
+    for _ in range(2):
+        leaves = [a.detach().clone().requires_grad_() for a in args]
+        y = fn(*leaves, residual=True)
+        y.backward(dy)
+        grads.append([y.detach()] + [l.grad for l in leaves])
+    for a, b in zip(*grads):
+        assert torch.equal(a, b)
+
+
+def test_device_error_word_clear(cuda_device):
+    from dynamic_conv1d_b200 import _lib
+
+    x = torch.zeros(1, device="cuda")
+    _lib.check_device(x)  # no bounded wait has given up

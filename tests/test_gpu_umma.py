@@ -1,0 +1,52 @@
+"""GPU: tcgen05.mma descriptor encodings of the lowrank tensor-core kernels.
+
+Each case stages bf16 operands into the exact no-swizzle shared-memory layouts
+that one MMA of the lowrank kernels uses (K-major or MN-major, SBO/LBO strides,
+row-shifted B) and compares D = A @ B with a float32 torch matmul."""
+from __future__ import annotations
+
+import ctypes
+import zlib
+
+import pytest
+import torch
+
+from dynamic_conv1d_b200 import _lib
+
+pytestmark = pytest.mark.gpu
+
+# name: (M, N, K, Nb, a_major, a_sbo, a_lbo, b_major, b_sbo, b_lbo, b_row_offset)
+CASES = {
+    # forward / dx weight generation: A = U_w^T [128 ch x R] K-major, B = z [tok x R] K-major
+    "fwd_R16": (128, 64, 16, 64, 0, 256, 128, 0, 128, 64 * 16, 0),
+    "fwd_R32": (128, 64, 32, 64, 0, 512, 128, 0, 128, 64 * 16, 0),
+    # dx: the same z buffer read from row w (shifted start address)
+    "dx_shift1": (128, 64, 16, 72, 0, 256, 128, 0, 128, 72 * 16, 1),
+    "dx_shift3": (128, 64, 16, 72, 0, 256, 128, 0, 128, 72 * 16, 3),
+    # dU: A = P^T [128 ch x 64 tok] K-major, B = z [64 tok x R] MN-major (the z buffer)
+    "dU_R16": (128, 16, 64, 16, 0, 1024, 128, 1, 72 * 16, 128, 0),
+    "dU_R32": (128, 32, 64, 32, 0, 1024, 128, 1, 72 * 16, 128, 0),
+    # dz: A = P [64 tok x 128 ch] MN-major (M = 64), B = U [128 ch x R] MN-major
+    "dz_R16": (64, 16, 128, 16, 1, 128, 1024, 1, 128, 256, 0),
+    "dz_R32": (64, 32, 128, 32, 1, 128, 1024, 1, 128, 512, 0),
+    # wide N, two K steps
+    "wide": (128, 256, 32, 256, 0, 512, 128, 0, 512, 128, 0),
+}
+
+
+@pytest.mark.parametrize("name", list(CASES))
+def test_umma_layout(name, cuda_device):
+    M, N, K, Nb, am, asbo, albo, bm, bsbo, blbo, off = CASES[name]
+    g = torch.Generator(device="cuda").manual_seed(zlib.crc32(name.encode()))
+    A = torch.randn(M, K, device="cuda", generator=g).to(torch.bfloat16)
+    B = torch.randn(K, Nb, device="cuda", generator=g).to(torch.bfloat16)
+    D = torch.full((M, N), float("nan"), device="cuda", dtype=torch.float32)
+    lib = _lib.load()
+    st = lib.dynconv_umma_selftest(
+        ctypes.c_void_p(A.data_ptr()), ctypes.c_void_p(B.data_ptr()), ctypes.c_void_p(D.data_ptr()),
+        M, N, K, Nb, am, asbo, albo, bm, bsbo, blbo, off, _lib.stream_of(A),
+    )
+    _lib.check(st)
+    _lib.check_device(A)
+    ref = A.float() @ B.float()[:, off:off + N]
+    torch.testing.assert_close(D, ref, atol=1e-3, rtol=1e-3)
