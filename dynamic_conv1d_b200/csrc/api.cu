@@ -66,6 +66,7 @@ int lr_bwd_simple_launch(const void* x, const void* z, const void* U, const void
 int umma_selftest_launch(const void* A, const void* B, float* D, int M, int N, int K, int Nb, int a_major, int a_sbo,
                          int a_lbo, int b_major, int b_sbo, int b_lbo, int b_off, cudaStream_t st);
 bool lr_tc_supported(int64_t D, int Rk, int W, int dtype, const void* const* ptrs, int nptrs);
+bool lr_tc_bwd_supported(int64_t D, int Rk, int W, int dtype, const void* const* ptrs, int nptrs);
 size_t lr_tc_bwd_workspace(int64_t B, int64_t T, int64_t D, int Rk, int W);
 int lr_tc_fwd_launch(const void* x, const void* z, const void* U, const void* sw, void* y, int64_t B, int64_t T,
                      int64_t D, int R, int Rk, int W, int residual, cudaStream_t st);
@@ -223,7 +224,7 @@ size_t dynconv_lr_bwd_workspace_bytes(int64_t B, int64_t T, int64_t D, int64_t R
   // which only ever moves a call onto the simple path; both fit the max).
   const size_t simple = align_up((size_t)lr_simple_partial_rows(B, T) * (size_t)Rk * (size_t)W * (size_t)D * sizeof(float));
   size_t tc = 0;
-  if (lr_tc_supported(D, Rk, (int)W, dtype, nullptr, 0)) tc = lr_tc_bwd_workspace(B, T, D, Rk, (int)W);
+  if (lr_tc_bwd_supported(D, Rk, (int)W, dtype, nullptr, 0)) tc = lr_tc_bwd_workspace(B, T, D, Rk, (int)W);
   return simple > tc ? simple : tc;
 }
 
@@ -250,7 +251,7 @@ int dynconv_lr_bwd(const void* x, const void* z, const void* U, const void* stat
   if (!workspace || workspace_bytes < need)
     return set_error(DYNCONV_ERR_WORKSPACE, "lr_bwd: workspace %zu < %zu bytes", workspace_bytes, need);
   const void* ptrs[] = {x, z, U, static_w, dy, dx, dz};
-  if (lr_tc_supported(D, Rk, (int)W, dtype, ptrs, 7))
+  if (lr_tc_bwd_supported(D, Rk, (int)W, dtype, ptrs, 7))
     return lr_tc_bwd_launch(x, z, U, static_w, dy, dx, dz, dU_f32, dU, dstatic_w, workspace, workspace_bytes, B, T, D,
                             (int)R, Rk, (int)W, residual, st);
   float* part = (float*)workspace;

@@ -191,6 +191,7 @@ constexpr uint32_t kMaxPolls = 1u << 26;
 
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, unsigned int site,
                                           volatile int* abort_flag) {
+  if (*abort_flag) return false;
   for (uint32_t i = 0; i < kMaxPolls; ++i) {
     if (mbar_try_wait(bar, parity)) return true;
     if ((i & 1023u) == 1023u && *abort_flag) return false;
