@@ -68,8 +68,9 @@ int umma_selftest_launch(const void* A, const void* B, float* D, int M, int N, i
 bool lr_tc_supported(int64_t D, int Rk, int W, int dtype, const void* const* ptrs, int nptrs);
 bool lr_tc_bwd_supported(int64_t D, int Rk, int W, int dtype, const void* const* ptrs, int nptrs);
 size_t lr_tc_bwd_workspace(int64_t B, int64_t T, int64_t D, int Rk, int W);
-int lr_tc_fwd_launch(const void* x, const void* z, const void* U, const void* sw, void* y, int64_t B, int64_t T,
-                     int64_t D, int R, int Rk, int W, int residual, cudaStream_t st);
+size_t lr_tc_fwd_workspace(int64_t B, int64_t T, int Rk);
+int lr_tc_fwd_launch(const void* x, const void* z, const void* U, const void* sw, void* y, void* ws, size_t ws_bytes,
+                     int64_t B, int64_t T, int64_t D, int R, int Rk, int W, int residual, cudaStream_t st);
 int lr_tc_bwd_launch(const void* x, const void* z, const void* U, const void* sw, const void* dy, void* dx, void* dz,
                      float* dU_f32, void* dU, void* dsw, void* ws, size_t ws_bytes, int64_t B, int64_t T, int64_t D,
                      int R, int Rk, int W, int residual, cudaStream_t st);
@@ -201,8 +202,16 @@ static int lr_checks(int64_t B, int64_t T, int64_t D, int64_t R, int64_t W, int 
   return DYNCONV_OK;
 }
 
-int dynconv_lr_fwd(const void* x, const void* z, const void* U, const void* static_w, void* y, int64_t B, int64_t T,
-                   int64_t D, int64_t R, int64_t W, int dtype, int residual, void* stream) {
+size_t dynconv_lr_fwd_workspace_bytes(int64_t B, int64_t T, int64_t D, int64_t R, int64_t W, int dtype,
+                                      int has_static) {
+  const int Rk = (int)R + (has_static ? 1 : 0);
+  if (B * T == 0 || !lr_tc_supported(D, Rk, (int)W, dtype, nullptr, 0)) return 0;
+  return lr_tc_fwd_workspace(B, T, Rk);
+}
+
+int dynconv_lr_fwd(const void* x, const void* z, const void* U, const void* static_w, void* y, void* workspace,
+                   size_t workspace_bytes, int64_t B, int64_t T, int64_t D, int64_t R, int64_t W, int dtype,
+                   int residual, void* stream) {
   int s;
   if ((s = lr_checks(B, T, D, R, W, dtype))) return s;
   const int Rk = (int)R + (static_w ? 1 : 0);
@@ -210,9 +219,14 @@ int dynconv_lr_fwd(const void* x, const void* z, const void* U, const void* stat
   if (B * T == 0) return DYNCONV_OK;
   if (!x || !z || !U || !y) return set_error(DYNCONV_ERR_ARGUMENT, "lr_fwd: null tensor");
   cudaStream_t st = (cudaStream_t)stream;
-  const void* ptrs[] = {x, z, U, static_w, y};
-  if (lr_tc_supported(D, Rk, (int)W, dtype, ptrs, 5))
-    return lr_tc_fwd_launch(x, z, U, static_w, y, B, T, D, (int)R, Rk, (int)W, residual, st);
+  const void* ptrs[] = {x, z, U, static_w, y, workspace};
+  if (lr_tc_supported(D, Rk, (int)W, dtype, ptrs, 6)) {
+    const size_t need = lr_tc_fwd_workspace(B, T, Rk);
+    if (!workspace || workspace_bytes < need)
+      return set_error(DYNCONV_ERR_WORKSPACE, "lr_fwd: workspace %zu < %zu bytes", workspace_bytes, need);
+    return lr_tc_fwd_launch(x, z, U, static_w, y, workspace, workspace_bytes, B, T, D, (int)R, Rk, (int)W, residual,
+                            st);
+  }
   return lr_fwd_simple_launch(x, z, U, static_w, y, B, T, D, (int)R, Rk, (int)W, dtype, residual, st);
 }
 

@@ -7,7 +7,10 @@
 // Forward data flow per work item (128 channels x 64 timesteps of one batch row):
 //
 //   HBM x  --TMA (3-D box, zero fill for t<0 / t>=T)--> smem x tile [67 rows][128 ch]
-//   HBM z  --producer warp (plain loads, static rank = 1.0)--> smem z tile, K-major
+//   HBM z_pack --TMA (4-D box)--> smem z tile, already in the K-major MMA layout
+//        (z_pack = z_ext as [R_kernel/8][B][T][8] bf16 with the static rank = 1.0,
+//         written once per call by z_pack_kernel; z rows are 2R bytes, which TMA
+//         cannot tile directly when R is odd)
 //   smem U (per 128-channel block, static_w folded as rank R)   [K-major, per tap]
 //   tcgen05.mma (M = 128 channels, N = 64 timesteps, K = R_kernel) per tap w
 //        -> TMEM acc_w[ch][t] = sum_r U[r,w,ch] z[t,r]      (the dynamic weights;
@@ -29,13 +32,17 @@ namespace dynconv {
 
 DYNCONV_DEFINE_ERROR_ACCESSOR(lr_tc_error_word)
 
+int reduce_partials_launch(const float* part, int P, int64_t n, float* out_f32, void* out, int dtype, cudaStream_t st);
+int cast_f32_launch(const float* src, void* dst, int64_t n, int dtype, cudaStream_t st);
+
 namespace {
 
 constexpr int kBT = 64;         // timesteps per work item (MMA N)
 constexpr int kBD = 128;        // channels per work item (MMA M)
-constexpr int kStages = 4;      // x/z pipeline depth
+constexpr int kStages = 4;      // x/z pipeline depth (forward, R_kernel <= 32)
 constexpr int kEpiWarps = 8;    // epilogue warps
 constexpr int kFwdThreads = 64 + 32 * kEpiWarps;
+
 
 // --------------------------------------------------------------- tensor maps
 
@@ -71,26 +78,81 @@ int make_btd_map(CUtensorMap* map, const void* base, int64_t B, int64_t T, int64
   return DYNCONV_OK;
 }
 
-// ------------------------------------------------------------- work split
+// 4-D bf16 map over z_pack [RKP/8][B][T][8]: dims (8, T, B, RKP/8), box (8, rows, 1, RKP/8).
+// The box lands in shared memory as [RKP/8][rows][8]: the no-swizzle K-major layout
+// (16-byte rows, 8-rank chunks `rows * 16` bytes apart).  Rows past T read as zero.
+int make_zpack_map(CUtensorMap* map, const void* base, int64_t B, int64_t T, int rkp, int rows) {
+  EncodeTiledFn fn = encode_fn();
+  if (!fn) return set_error(DYNCONV_ERR_CUDA, "cuTensorMapEncodeTiled unavailable");
+  cuuint64_t dims[4] = {8, (cuuint64_t)T, (cuuint64_t)B, (cuuint64_t)(rkp / 8)};
+  cuuint64_t strides[3] = {16, (cuuint64_t)T * 16, (cuuint64_t)B * T * 16};
+  cuuint32_t box[4] = {8, (cuuint32_t)rows, 1, (cuuint32_t)(rkp / 8)};
+  cuuint32_t estr[4] = {1, 1, 1, 1};
+  CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 4, const_cast<void*>(base), dims, strides, box, estr,
+                  CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_128B,
+                  CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return set_error(DYNCONV_ERR_CUDA, "cuTensorMapEncodeTiled(z_pack) failed (%d)", (int)r);
+  return DYNCONV_OK;
+}
 
-struct WorkSplit {
-  int n_dblk;       // 128-channel blocks
-  int tiles_row;    // 64-step tiles per batch row
-  int64_t n_items;  // n_dblk * B * tiles_row, d-block major
+// z_pack[c][b][t][e] = z_ext[b, t, 8c + e]: z for ranks < R, 1.0 at rank R when the
+// static filter is fused (the reference's F.pad(z, (0, 1), value=1.0),
+// lowrank.py:224), 0 up to RKP.  One thread per (b, t).
+__global__ void __launch_bounds__(256) z_pack_kernel(const __nv_bfloat16* __restrict__ z,
+                                                     __nv_bfloat16* __restrict__ zp, int64_t ntok, int R, int rkp,
+                                                     int has_static) {
+  const int64_t tok = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (tok >= ntok) return;
+  const __nv_bfloat16* zr = z + tok * R;
+  for (int c = 0; c < rkp / 8; ++c) {
+    __align__(16) __nv_bfloat16 v[8];
+#pragma unroll
+    for (int e = 0; e < 8; ++e) {
+      const int r = 8 * c + e;
+      v[e] = r < R ? zr[r] : __float2bfloat16_rn((r == R && has_static) ? 1.f : 0.f);
+    }
+    *reinterpret_cast<uint4*>(zp + ((size_t)c * ntok + tok) * 8) = *reinterpret_cast<const uint4*>(v);
+  }
+}
+
+size_t zpack_bytes(int64_t B, int64_t T, int rkp) { return ((size_t)B * T * rkp * 2 + 255) / 256 * 256; }
+
+int z_pack_launch(const void* z, void* zp, int64_t B, int64_t T, int R, int rkp, bool has_static, cudaStream_t st) {
+  const int64_t ntok = B * T;
+  z_pack_kernel<<<(unsigned)((ntok + 255) / 256), 256, 0, st>>>((const __nv_bfloat16*)z, (__nv_bfloat16*)zp, ntok, R,
+                                                               rkp, has_static ? 1 : 0);
+  DYNCONV_CHECK_LAUNCH("z_pack_kernel");
+  return DYNCONV_OK;
+}
+
+// ------------------------------------------------------------- work split
+//
+// CTA (dblk, g) of a grid of n_dblk x n_groups owns channel block dblk (128
+// channels) for the contiguous range of 64-step tiles [j0, j1) of group g, tiles
+// numbered b * tiles_row + t0 / 64.  A fixed channel block per CTA means the U
+// block is loaded once, and the CTAs of one tile (one per channel block) run in
+// step -- which the backward's cross-CTA dz reduction relies on.
+struct TileSplit {
+  int n_dblk, n_groups, tiles_row, n_tiles;
 };
 
-__host__ __device__ inline void item_coords(const WorkSplit& w, int64_t item, int& dblk, int& b, int& t0) {
-  const int64_t tiles = w.n_items / w.n_dblk;  // B * tiles_row
-  dblk = (int)(item / tiles);
-  const int64_t tile = item % tiles;
-  b = (int)(tile / w.tiles_row);
-  t0 = (int)(tile % w.tiles_row) * kBT;
+TileSplit tile_split(int64_t B, int64_t T, int64_t D) {
+  TileSplit sp;
+  sp.n_dblk = (int)((D + kBD - 1) / kBD);
+  sp.tiles_row = (int)((T + kBT - 1) / kBT);
+  sp.n_tiles = (int)(B * sp.tiles_row);
+  int ng = sm_count() / sp.n_dblk;
+  if (ng < 1) ng = 1;
+  if (ng > sp.n_tiles) ng = sp.n_tiles;
+  sp.n_groups = ng;
+  return sp;
 }
 
 // ------------------------------------------------------------- smem layout
 
 template <int W, int RKP>
 struct FwdSmem {
+  static constexpr int kS = RKP <= 32 ? kStages : 3;  // pipeline depth (shared memory bound)
   static constexpr int kXRows = kBT + W - 1;
   static constexpr uint32_t kXBytes = (uint32_t)kXRows * kBD * 2;        // TMA box bytes
   static constexpr uint32_t kXStride = (kXBytes + 1023u) / 1024u * 1024u;
@@ -98,8 +160,8 @@ struct FwdSmem {
   static constexpr uint32_t kYBytes = (uint32_t)kBT * kBD * 2;
   static constexpr uint32_t kUTap = (uint32_t)kBD * RKP * 2;
   static constexpr uint32_t kOffX = 0;
-  static constexpr uint32_t kOffZ = kOffX + kStages * kXStride;
-  static constexpr uint32_t kOffY = kOffZ + kStages * kZBytes;
+  static constexpr uint32_t kOffZ = kOffX + kS * kXStride;
+  static constexpr uint32_t kOffY = kOffZ + kS * kZBytes;
   static constexpr uint32_t kOffU = kOffY + 2 * kYBytes;
   static constexpr uint32_t kTotal = kOffU + W * kUTap + 1024;  // + alignment slack
   // K-major operand strides
@@ -109,49 +171,30 @@ struct FwdSmem {
   static constexpr uint32_t kUSbo = (RKP / 8) * 128;   // next 8 channels
 };
 
-// Loads U_ext for channel block dblk into smem (K-major, one [128 x RKP] block per tap).
+// Loads U_ext for channel block dblk into smem: one [128 ch x RKP] K-major block per
+// tap (rank R = static_w when present, zero padding up to RKP).  All `nthreads`
+// threads take part; each reads 16-byte vectors (8 channels of one (rank, tap) row;
+// D % 8 == 0 on this path, so a vector never straddles the end of D).
 template <int W, int RKP>
 __device__ void load_u_block(uint8_t* us, const __nv_bfloat16* __restrict__ U, const __nv_bfloat16* __restrict__ sw,
-                             int dblk, int D, int R, int lane, int nthreads) {
-  using L = FwdSmem<W, RKP>;
+                             int dblk, int D, int R, int tid, int nthreads) {
+  constexpr uint32_t kUTap = (uint32_t)kBD * RKP * 2;
+  constexpr uint32_t kUSbo = (RKP / 8) * 128;
   const int d0 = dblk * kBD;
-  for (int e = lane; e < W * RKP * kBD; e += nthreads) {
-    const int d = e % kBD;
-    const int r = (e / kBD) % RKP;
-    const int w = e / (kBD * RKP);
-    __nv_bfloat16 v = __float2bfloat16_rn(0.f);
-    if (d0 + d < D) {
-      if (r < R) v = U[((size_t)r * W + w) * D + d0 + d];
-      else if (r == R && sw != nullptr) v = sw[(size_t)w * D + d0 + d];
+  for (int e = tid; e < W * RKP * (kBD / 8); e += nthreads) {
+    const int v8 = e % (kBD / 8);  // 8-channel group
+    const int r = (e / (kBD / 8)) % RKP;
+    const int w = e / ((kBD / 8) * RKP);
+    const int d = d0 + v8 * 8;
+    uint4 u = make_uint4(0, 0, 0, 0);
+    if (d < D) {
+      if (r < R) u = __ldg(reinterpret_cast<const uint4*>(U + ((size_t)r * W + w) * D + d));
+      else if (r == R && sw != nullptr) u = __ldg(reinterpret_cast<const uint4*>(sw + (size_t)w * D + d));
     }
-    *reinterpret_cast<__nv_bfloat16*>(us + w * L::kUTap + kmajor_off(d, r, L::kUSbo, L::kULbo)) = v;
-  }
-}
-
-// Writes the z tile (64 timesteps x RKP ranks, K-major) for rows t0.. of batch b.
-template <int W, int RKP>
-__device__ void load_z_tile(uint8_t* zs, const __nv_bfloat16* __restrict__ z, int b, int t0, int T, int R,
-                            bool has_static, int lane) {
-  using L = FwdSmem<W, RKP>;
-  for (int j = lane; j < kBT; j += 32) {
-    const int t = t0 + j;
-    const bool ok = t < T;
-    const __nv_bfloat16* zr = z + ((size_t)b * T + (ok ? t : 0)) * R;
+    const __nv_bfloat16* h = reinterpret_cast<const __nv_bfloat16*>(&u);
 #pragma unroll
-    for (int c = 0; c < RKP / 8; ++c) {
-      __align__(16) __nv_bfloat16 v[8];
-#pragma unroll
-      for (int k = 0; k < 8; ++k) {
-        const int r = c * 8 + k;
-        float f = 0.f;
-        if (ok) {
-          if (r < R) f = __bfloat162float(zr[r]);
-          else if (r == R && has_static) f = 1.f;
-        }
-        v[k] = __float2bfloat16_rn(f);
-      }
-      *reinterpret_cast<uint4*>(zs + kmajor_off(j, c * 8, L::kZSbo, L::kZLbo)) = *reinterpret_cast<uint4*>(v);
-    }
+    for (int i = 0; i < 8; ++i)
+      *reinterpret_cast<__nv_bfloat16*>(us + w * kUTap + kmajor_off(v8 * 8 + i, r, kUSbo, 128)) = h[i];
   }
 }
 
@@ -160,39 +203,46 @@ __device__ void load_z_tile(uint8_t* zs, const __nv_bfloat16* __restrict__ z, in
 template <int W, int RKP>
 __global__ void __launch_bounds__(kFwdThreads, 1)
     lr_fwd_tc_kernel(const __grid_constant__ CUtensorMap xmap, const __grid_constant__ CUtensorMap ymap,
-                     const __nv_bfloat16* __restrict__ z, const __nv_bfloat16* __restrict__ U,
-                     const __nv_bfloat16* __restrict__ sw, WorkSplit ws, int T, int D, int R, int residual) {
+                     const __grid_constant__ CUtensorMap zmap, const __nv_bfloat16* __restrict__ U,
+                     const __nv_bfloat16* __restrict__ sw, TileSplit sp, int T, int D, int R, int residual) {
   using L = FwdSmem<W, RKP>;
   extern __shared__ uint8_t smem_raw[];
-  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  __shared__ uint64_t full_bar[kStages], empty_bar[kStages], accf_bar[2], acce_bar[2], u_bar;
+  uint8_t* smem = align_smem_1024(smem_raw);
+  constexpr int S = L::kS;
+  __shared__ uint64_t full_bar[S], empty_bar[S], accf_bar[2], acce_bar[2];
   __shared__ uint32_t tmem_slot;
   __shared__ int abort_flag;
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int64_t G = gridDim.x;
-  const int64_t it0 = ws.n_items * blockIdx.x / G, it1 = ws.n_items * (blockIdx.x + 1) / G;
+  const int dblk = blockIdx.x % sp.n_dblk;
+  const int g = blockIdx.x / sp.n_dblk;
+  const int j0 = (int)((int64_t)sp.n_tiles * g / sp.n_groups);
+  const int n = (int)((int64_t)sp.n_tiles * (g + 1) / sp.n_groups) - j0;
+  const int d0 = dblk * kBD;
   const bool has_static = sw != nullptr;
   constexpr uint32_t kAccCols = W * kBT;
   constexpr uint32_t kTmemCols = (2 * kAccCols <= 256) ? 256 : 512;
 
   if (threadIdx.x == 0) {
-    for (int s = 0; s < kStages; ++s) {
-      mbar_init(&full_bar[s], 1);
+    for (int s = 0; s < S; ++s) {
+      mbar_init(&full_bar[s], 1);  // one arrive.expect_tx; the x and z TMA loads complete the bytes
       mbar_init(&empty_bar[s], kEpiWarps);
     }
     for (int a = 0; a < 2; ++a) {
       mbar_init(&accf_bar[a], 1);
       mbar_init(&acce_bar[a], kEpiWarps);
     }
-    mbar_init(&u_bar, 1);
     abort_flag = 0;
     fence_barrier_init();
   }
   if (warp == 0 && lane == 0) {
     prefetch_tensormap(&xmap);
     prefetch_tensormap(&ymap);
+    prefetch_tensormap(&zmap);
   }
+  // U block of this CTA's channels, loaded once by every thread (MMA A operand).
+  load_u_block<W, RKP>(smem + L::kOffU, U, sw, dblk, D, R, threadIdx.x, blockDim.x);
+  fence_proxy_async_smem();
   if (warp == 1) {
     tmem_alloc(&tmem_slot, kTmemCols);
     tmem_relinquish();
@@ -204,43 +254,25 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
 
   if (warp == 0) {
     // ------------------------------------------------------------ producer
-    const uint64_t pol = policy_evict_first();
-    for (int64_t i = it0; i < it1; ++i) {
-      const int k = (int)(i - it0), s = k % kStages;
-      if (!mbar_wait(&empty_bar[s], ((k / kStages) & 1) ^ 1, kErrWaitProducer, &abort_flag)) break;
-      int dblk, b, t0;
-      item_coords(ws, i, dblk, b, t0);
-      load_z_tile<W, RKP>(smem + L::kOffZ + s * L::kZBytes, z, b, t0, T, R, has_static, lane);
-      fence_proxy_async_smem();
-      __syncwarp();
-      if (lane == 0) {
-        mbar_arrive_expect_tx(&full_bar[s], L::kXBytes);
-        tma_load_3d(smem + L::kOffX + s * L::kXStride, &xmap, &full_bar[s], dblk * kBD, t0 - (W - 1), b, pol);
+    if (lane == 0) {
+      const uint64_t pol = policy_evict_first();
+      for (int k = 0; k < n; ++k) {
+        const int s = k % S;
+        if (!mbar_wait(&empty_bar[s], ((k / S) & 1) ^ 1, kErrWaitProducer, &abort_flag)) break;
+        const int tile = j0 + k, b = tile / sp.tiles_row, t0 = (tile % sp.tiles_row) * kBT;
+        mbar_arrive_expect_tx(&full_bar[s], L::kXBytes + L::kZBytes);
+        tma_load_3d(smem + L::kOffX + s * L::kXStride, &xmap, &full_bar[s], d0, t0 - (W - 1), b, pol);
+        tma_load_4d(smem + L::kOffZ + s * L::kZBytes, &zmap, &full_bar[s], 0, t0, b, 0, pol);
       }
     }
+    __syncwarp();
   } else if (warp == 1) {
     // ------------------------------------------------------------ MMA issuer
     const uint32_t idesc = make_idesc_bf16(kBD, kBT, 0, 0);
     uint8_t* us = smem + L::kOffU;
-    int cur = -1;
-    uint32_t u_phase = 0;
-    for (int64_t i = it0; i < it1; ++i) {
-      const int k = (int)(i - it0), s = k % kStages, a = k & 1;
-      int dblk, b, t0;
-      item_coords(ws, i, dblk, b, t0);
-      if (dblk != cur) {
-        if (cur >= 0) {  // wait until the MMAs that read the old U block are done
-          if (lane == 0) umma_commit(&u_bar);
-          __syncwarp();
-          if (!mbar_wait(&u_bar, u_phase, kErrWaitMma, &abort_flag)) break;
-          u_phase ^= 1;
-        }
-        load_u_block<W, RKP>(us, U, sw, dblk, D, R, lane, 32);
-        fence_proxy_async_smem();
-        __syncwarp();
-        cur = dblk;
-      }
-      if (!mbar_wait(&full_bar[s], (k / kStages) & 1, kErrWaitMma, &abort_flag)) break;
+    for (int k = 0; k < n; ++k) {
+      const int s = k % S, a = k & 1;
+      if (!mbar_wait(&full_bar[s], (k / S) & 1, kErrWaitMma, &abort_flag)) break;
       if (!mbar_wait(&acce_bar[a], ((k >> 1) & 1) ^ 1, kErrWaitMma, &abort_flag)) break;
       tc_fence_after();
       if (lane == 0) {
@@ -268,14 +300,13 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
     const int et = e * 32 + lane;      // 0..255
     const uint64_t pol_y = policy_evict_first();
     bool dead = false;  // a bounded wait gave up: keep joining the named barriers, skip the work
-    for (int64_t i = it0; i < it1; ++i) {
-      const int k = (int)(i - it0), s = k % kStages, a = k & 1;
-      int dblk, b, t0;
-      item_coords(ws, i, dblk, b, t0);
+    for (int k = 0; k < n; ++k) {
+      const int s = k % S, a = k & 1;
+      const int tile = j0 + k, b = tile / sp.tiles_row, t0 = (tile % sp.tiles_row) * kBT;
       // y buffer `a` is free once the store issued two items ago has read it
       if (et == 0 && !dead) bulk_wait_group_read<1>();
       named_bar_sync(1, 32 * kEpiWarps);
-      if (!dead) dead = !mbar_wait(&full_bar[s], (k / kStages) & 1, kErrWaitEpilogue, &abort_flag);
+      if (!dead) dead = !mbar_wait(&full_bar[s], (k / S) & 1, kErrWaitEpilogue, &abort_flag);
       if (!dead) dead = !mbar_wait(&accf_bar[a], (k >> 1) & 1, kErrWaitEpilogue, &abort_flag);
       tc_fence_after();
       __nv_bfloat16* ys = reinterpret_cast<__nv_bfloat16*>(smem + L::kOffY + a * L::kYBytes);
@@ -317,7 +348,7 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
       fence_proxy_async_smem();
       named_bar_sync(1, 32 * kEpiWarps);
       if (et == 0 && !dead) {
-        tma_store_3d(&ymap, ys, dblk * kBD, t0, b, pol_y);
+        tma_store_3d(&ymap, ys, d0, t0, b, pol_y);
         bulk_commit_group();
       }
     }
@@ -330,37 +361,468 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
 }
 
 template <int W, int RKP>
-int launch_fwd(const void* x, const void* z, const void* U, const void* sw, void* y, int64_t B, int64_t T, int64_t D,
-               int R, int residual, cudaStream_t st) {
+int launch_fwd(const void* x, const void* z, const void* U, const void* sw, void* y, void* ws, int64_t B, int64_t T,
+               int64_t D, int R, int residual, cudaStream_t st) {
   using L = FwdSmem<W, RKP>;
-  CUtensorMap xmap, ymap;
+  static_assert(L::kTotal <= 232448 - 512, "forward shared memory budget (227 KB per CTA)");
+  CUtensorMap xmap, ymap, zmap;
   int s;
   if ((s = make_btd_map(&xmap, x, B, T, D, kBD, kBT + W - 1))) return s;
   if ((s = make_btd_map(&ymap, y, B, T, D, kBD, kBT))) return s;
-  WorkSplit ws;
-  ws.n_dblk = (int)((D + kBD - 1) / kBD);
-  ws.tiles_row = (int)((T + kBT - 1) / kBT);
-  ws.n_items = (int64_t)ws.n_dblk * B * ws.tiles_row;
-  const int grid = (int)std::min<int64_t>(ws.n_items, sm_count());
+  if ((s = make_zpack_map(&zmap, ws, B, T, RKP, kBT))) return s;
+  if ((s = z_pack_launch(z, ws, B, T, R, RKP, sw != nullptr, st))) return s;
+  const TileSplit sp = tile_split(B, T, D);
+  const int grid = sp.n_dblk * sp.n_groups;
   const int smem = (int)L::kTotal;
   cudaError_t e = cudaFuncSetAttribute(lr_fwd_tc_kernel<W, RKP>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
-  if (e != cudaSuccess) return cuda_status(e, "cudaFuncSetAttribute(lr_fwd_tc)");
-  lr_fwd_tc_kernel<W, RKP><<<grid, kFwdThreads, smem, st>>>(xmap, ymap, (const __nv_bfloat16*)z,
-                                                            (const __nv_bfloat16*)U, (const __nv_bfloat16*)sw, ws,
-                                                            (int)T, (int)D, R, residual);
+  if (e != cudaSuccess) {
+    cudaGetLastError();  // do not leave the failure pending for the next launch check
+    return cuda_status(e, "cudaFuncSetAttribute(lr_fwd_tc)");
+  }
+  lr_fwd_tc_kernel<W, RKP><<<grid, kFwdThreads, smem, st>>>(xmap, ymap, zmap, (const __nv_bfloat16*)U,
+                                                            (const __nv_bfloat16*)sw, sp, (int)T, (int)D, R, residual);
   DYNCONV_CHECK_LAUNCH("lr_fwd_tc_kernel");
   return DYNCONV_OK;
 }
 
 template <int RKP>
-int launch_fwd_w(int W, const void* x, const void* z, const void* U, const void* sw, void* y, int64_t B, int64_t T,
-                 int64_t D, int R, int residual, cudaStream_t st) {
+int launch_fwd_w(int W, const void* x, const void* z, const void* U, const void* sw, void* y, void* ws, int64_t B,
+                 int64_t T, int64_t D, int R, int residual, cudaStream_t st) {
   switch (W) {
-    case 1: return launch_fwd<1, RKP>(x, z, U, sw, y, B, T, D, R, residual, st);
-    case 2: return launch_fwd<2, RKP>(x, z, U, sw, y, B, T, D, R, residual, st);
-    case 3: return launch_fwd<3, RKP>(x, z, U, sw, y, B, T, D, R, residual, st);
-    case 4: return launch_fwd<4, RKP>(x, z, U, sw, y, B, T, D, R, residual, st);
+    case 1: return launch_fwd<1, RKP>(x, z, U, sw, y, ws, B, T, D, R, residual, st);
+    case 2: return launch_fwd<2, RKP>(x, z, U, sw, y, ws, B, T, D, R, residual, st);
+    case 3: return launch_fwd<3, RKP>(x, z, U, sw, y, ws, B, T, D, R, residual, st);
+    case 4: return launch_fwd<4, RKP>(x, z, U, sw, y, ws, B, T, D, R, residual, st);
     default: return set_error(DYNCONV_ERR_UNSUPPORTED, "tensor-core path: W=%d", W);
+  }
+}
+
+
+// ============================================================== backward
+//
+// One fused pass over dy and x per work item (128 channels x 64 timesteps):
+//
+//   MMA-1  acc1_w[ch][t] = sum_r U[r,w,ch] z[t+w,r]    M=128 ch, N=32 t (two halves), K=R_kernel
+//          (B = the z tile read from row w: the no-swizzle K-major layout is linear in rows)
+//   epilogue: dx[t,ch] = sum_w acc1_w[ch][t] dy[t+w,ch] (+ dy)   -> HBM (bf16)
+//             P_w[t,ch] = bf16(dy[t,ch] x[t-w,ch])               -> smem (bf16, as the
+//             reference rounds dy*x to bf16 before its dots, lowrank.py:128)
+//   MMA-2  dU_w[ch][r] += sum_t P_w[t,ch] z[t,r]       M=128 ch, N=R_kernel, K=64 t
+//          (accumulated in TMEM over all items of the CTA; one partial row block per CTA)
+//   MMA-3  dz[t][r]     = sum_{w,ch} P_w[t,ch] U[r,w,ch] M=64 t,  N=R_kernel, K=128*W
+//          (partial over this CTA's 128 channels; the last of the channel-block CTAs
+//          of a tile, by an atomic ticket, sums the partials in channel-block order)
+//
+// The P buffer serves MMA-2 as a K-major A operand and MMA-3 as an MN-major A
+// operand; the z tile serves MMA-1 (K-major B) and MMA-2 (MN-major B); the U
+// block serves MMA-1 (K-major A) and MMA-3 (MN-major B): one smem copy each.
+// Grid = n_dblk x n_groups CTAs: CTA (dblk, g) owns channel block dblk for a
+// contiguous range of 64-step tiles, so the CTAs sharing a tile's dz run in step
+// and the dz partial working set stays small and L2-resident.
+
+constexpr int kBwdStages = 2;
+constexpr int kZRows = 72;  // z rows t0 .. t0+71 (64 + W-1 look-ahead, rounded up to whole core matrices)
+constexpr int kBwdThreads = 64 + 32 * kEpiWarps;
+
+__host__ __device__ constexpr uint32_t round1024(uint32_t v) { return (v + 1023u) / 1024u * 1024u; }
+
+template <int W, int RKP, int NP>
+struct BwdSmem {
+  static constexpr int kRows = kBT + W - 1;
+  static constexpr uint32_t kTileBytes = (uint32_t)kRows * kBD * 2;
+  static constexpr uint32_t kTileStride = round1024(kTileBytes);
+  static constexpr uint32_t kZBytes = (uint32_t)kZRows * RKP * 2;
+  static constexpr uint32_t kZStride = (kZBytes + 127u) / 128u * 128u;
+  static constexpr uint32_t kUTap = (uint32_t)kBD * RKP * 2;
+  static constexpr uint32_t kPTap = (uint32_t)kBT * kBD * 2;
+  static constexpr uint32_t kOffU = 0;
+  static constexpr uint32_t kOffDy = round1024(kOffU + W * kUTap);
+  static constexpr uint32_t kOffX = kOffDy + kBwdStages * kTileStride;
+  static constexpr uint32_t kOffZ = kOffX + kBwdStages * kTileStride;
+  static constexpr uint32_t kOffP = round1024(kOffZ + kBwdStages * kZStride);
+  static constexpr uint32_t kTotal = kOffP + NP * W * kPTap + 1024;
+  // no-swizzle operand strides (bytes)
+  static constexpr uint32_t kUChunk = (RKP / 8) * 128;  // U: next 8 channels (K-major sbo / MN-major lbo)
+  static constexpr uint32_t kZChunk = kZRows * 16;      // z: next 8 ranks
+  static constexpr uint32_t kPChunk = (kBT / 8) * 128;  // P: next 8 channels
+  // TMEM columns
+  static constexpr uint32_t kColA1 = 0;                       // 2 halves x W taps x 32
+  static constexpr uint32_t kColDU = 64 * W;                  // W x RKP
+  static constexpr uint32_t kColDZ = kColDU + W * RKP;        // 2 x RKP
+  static constexpr uint32_t kCols = kColDZ + 2 * RKP;
+  static constexpr uint32_t kAlloc = kCols <= 256 ? 256 : 512;
+  static_assert(kCols <= 512, "TMEM budget");
+};
+
+template <int N>
+__device__ __forceinline__ void tmem_ld_n(uint32_t taddr, float (&v)[N]) {
+  static_assert(N == 8 || N == 16, "");
+  if constexpr (N == 8) tmem_ld8(taddr, v);
+  else tmem_ld16(taddr, v);
+}
+
+template <int W, int RKP, int NP>
+__global__ void __launch_bounds__(kBwdThreads, 1)
+    lr_bwd_tc_kernel(const __grid_constant__ CUtensorMap dymap, const __grid_constant__ CUtensorMap xmap,
+                     const __grid_constant__ CUtensorMap zmap, const __nv_bfloat16* __restrict__ U,
+                     const __nv_bfloat16* __restrict__ sw, __nv_bfloat16* __restrict__ dx,
+                     __nv_bfloat16* __restrict__ dz, float* __restrict__ dzp, int* __restrict__ cnt,
+                     float* __restrict__ dUp, TileSplit sp, int T, int D, int R, int Rk, int residual) {
+  using L = BwdSmem<W, RKP, NP>;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = align_smem_1024(smem_raw);
+  __shared__ uint64_t full_bar[kBwdStages], empty_bar[kBwdStages], a1f_bar[2], a1e_bar[2], pf_bar[NP], pe_bar[NP],
+      dzf_bar[2], dze_bar[2], du_bar;
+  __shared__ uint32_t tmem_slot;
+  __shared__ int abort_flag;
+  __shared__ volatile int last_flag;
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int dblk = blockIdx.x % sp.n_dblk;
+  const int g = blockIdx.x / sp.n_dblk;
+  const int j0 = (int)((int64_t)sp.n_tiles * g / sp.n_groups);
+  const int j1 = (int)((int64_t)sp.n_tiles * (g + 1) / sp.n_groups);
+  const int n = j1 - j0;
+  const int d0 = dblk * kBD;
+  const bool has_static = sw != nullptr;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < kBwdStages; ++s) {
+      mbar_init(&full_bar[s], 1);  // one arrive.expect_tx; the dy, x and z TMA loads complete the bytes
+      mbar_init(&empty_bar[s], 1);
+    }
+    for (int h = 0; h < 2; ++h) {
+      mbar_init(&a1f_bar[h], 1);
+      mbar_init(&a1e_bar[h], kEpiWarps);
+      mbar_init(&dzf_bar[h], 1);
+      mbar_init(&dze_bar[h], kEpiWarps);
+    }
+    for (int p = 0; p < NP; ++p) {
+      mbar_init(&pf_bar[p], kEpiWarps);
+      mbar_init(&pe_bar[p], 1);
+    }
+    mbar_init(&du_bar, 1);
+    abort_flag = 0;
+    last_flag = 0;
+    fence_barrier_init();
+  }
+  if (warp == 0 && lane == 0) {
+    prefetch_tensormap(&dymap);
+    prefetch_tensormap(&xmap);
+    prefetch_tensormap(&zmap);
+  }
+  // U block of this CTA's channels (MMA-1 A operand, MMA-3 B operand), loaded once.
+  load_u_block<W, RKP>(smem + L::kOffU, U, sw, dblk, D, R, threadIdx.x, blockDim.x);
+  fence_proxy_async_smem();
+  if (warp == 1) {
+    tmem_alloc(&tmem_slot, L::kAlloc);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = tmem_slot;
+
+  if (warp == 0) {
+    // ------------------------------------------------------------ producer
+    // Stage k % 2 is released by the commit after the MMAs of tile k-2.
+    if (lane == 0) {
+      const uint64_t pol = policy_evict_first();
+      for (int k = 0; k < n; ++k) {
+        const int s = k % kBwdStages;
+        if (!mbar_wait(&empty_bar[s], ((k / kBwdStages) & 1) ^ 1, kErrWaitProducer, &abort_flag)) break;
+        const int tile = j0 + k, b = tile / sp.tiles_row, t0 = (tile % sp.tiles_row) * kBT;
+        mbar_arrive_expect_tx(&full_bar[s], 2 * L::kTileBytes + L::kZBytes);
+        tma_load_3d(smem + L::kOffDy + s * L::kTileStride, &dymap, &full_bar[s], d0, t0, b, pol);
+        tma_load_3d(smem + L::kOffX + s * L::kTileStride, &xmap, &full_bar[s], d0, t0 - (W - 1), b, pol);
+        tma_load_4d(smem + L::kOffZ + s * L::kZStride, &zmap, &full_bar[s], 0, t0, b, 0, pol);
+      }
+    }
+    __syncwarp();
+  } else if (warp == 1) {
+    // ------------------------------------------------------------ MMA issuer
+    uint8_t* us = smem + L::kOffU;
+    const uint32_t ub = smem_u32(us), pb0 = smem_u32(smem + L::kOffP);
+    const uint32_t idesc1 = make_idesc_bf16(kBD, 32, 0, 0);
+    const uint32_t idesc2 = make_idesc_bf16(kBD, RKP, 0, 1);
+    const uint32_t idesc3 = make_idesc_bf16(64, RKP, 1, 1);
+    bool ok = true;
+    auto mma23 = [&](int j) -> bool {
+      const int p = j % NP, sj = j % kBwdStages;
+      if (!mbar_wait(&pf_bar[p], (j / NP) & 1, kErrWaitMma, &abort_flag)) return false;
+      if (!mbar_wait(&dze_bar[j & 1], ((j >> 1) & 1) ^ 1, kErrWaitMma, &abort_flag)) return false;
+      tc_fence_after();
+      if (lane == 0) {
+        const uint32_t zb = smem_u32(smem + L::kOffZ + sj * L::kZStride);
+        const uint32_t pb = pb0 + p * W * L::kPTap;
+#pragma unroll
+        for (int w = 0; w < W; ++w) {
+#pragma unroll
+          for (int ks = 0; ks < kBT / 16; ++ks) {  // MMA-2: K = timesteps
+            const uint64_t ad = make_smem_desc(pb + w * L::kPTap + ks * 256, 128, L::kPChunk);
+            const uint64_t bd = make_smem_desc(zb + ks * 256, 128, L::kZChunk);
+            umma_f16(tmem + L::kColDU + w * RKP, ad, bd, idesc2, (j == 0 && ks == 0) ? 0u : 1u);
+          }
+        }
+#pragma unroll
+        for (int w = 0; w < W; ++w) {
+#pragma unroll
+          for (int ks = 0; ks < kBD / 16; ++ks) {  // MMA-3: K = (tap, channel)
+            const uint64_t ad = make_smem_desc(pb + w * L::kPTap + ks * 2 * L::kPChunk, L::kPChunk, 128);
+            const uint64_t bd = make_smem_desc(ub + w * L::kUTap + ks * 2 * L::kUChunk, L::kUChunk, 128);
+            umma_f16(tmem + L::kColDZ + (j & 1) * RKP, ad, bd, idesc3, (w == 0 && ks == 0) ? 0u : 1u);
+          }
+        }
+        umma_commit(&dzf_bar[j & 1]);
+        umma_commit(&pe_bar[p]);
+        umma_commit(&empty_bar[sj]);
+      }
+      __syncwarp();
+      return true;
+    };
+    for (int k = 0; k < n && ok; ++k) {
+      const int s = k % kBwdStages;
+      if (!mbar_wait(&full_bar[s], (k / kBwdStages) & 1, kErrWaitMma, &abort_flag)) break;
+      const uint32_t zb = smem_u32(smem + L::kOffZ + s * L::kZStride);
+      for (int h = 0; h < 2 && ok; ++h) {
+        if (!mbar_wait(&a1e_bar[h], (k & 1) ^ 1, kErrWaitMma, &abort_flag)) { ok = false; break; }
+        tc_fence_after();
+        if (lane == 0) {
+#pragma unroll
+          for (int w = 0; w < W; ++w) {
+#pragma unroll
+            for (int ks = 0; ks < RKP / 16; ++ks) {  // MMA-1: z rows from 32h + w
+              const uint64_t ad = make_smem_desc(ub + w * L::kUTap + ks * 256, 128, L::kUChunk);
+              const uint64_t bd = make_smem_desc(zb + (32 * h + w) * 16 + ks * 2 * L::kZChunk, L::kZChunk, 128);
+              umma_f16(tmem + L::kColA1 + h * 32 * W + w * 32, ad, bd, idesc1, ks > 0 ? 1u : 0u);
+            }
+          }
+          umma_commit(&a1f_bar[h]);
+        }
+        __syncwarp();
+      }
+      if (ok && k >= 1) ok = mma23(k - 1);
+    }
+    if (ok && n >= 1) ok = mma23(n - 1);
+    if (lane == 0) umma_commit(&du_bar);
+    __syncwarp();
+  } else {
+    // ------------------------------------------------------------ epilogue
+    const int e = warp - 2;
+    const int q = warp & 3;
+    const int pp = e >> 2;
+    const int ch = q * 32 + lane;
+    const int et = e * 32 + lane;
+    const bool dok = d0 + ch < D;
+    const uint32_t lane_base = (uint32_t)(q * 32) << 16;
+    bool dead = false;
+
+    auto dz_readout = [&](int j) {
+      const int tile = j0 + j, b = tile / sp.tiles_row, t0 = (tile % sp.tiles_row) * kBT;
+      if (!dead) dead = !mbar_wait(&dzf_bar[j & 1], (j >> 1) & 1, kErrWaitEpilogue, &abort_flag);
+      tc_fence_after();
+      constexpr int NH = RKP / 2;
+      float v[NH];
+      const int c0 = pp * NH;
+      if (!dead) {
+        tmem_ld_n<NH>(tmem + lane_base + L::kColDZ + (j & 1) * RKP + c0, v);
+        tmem_ld_wait();
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&dze_bar[j & 1]);
+      const int tok = 16 * q + lane;  // M = 64 layout: lanes 0..15 of each quarter
+      if (!dead && lane < 16) {
+        float* dst = dzp + (((size_t)dblk * sp.n_tiles + tile) * kBT + tok) * RKP + c0;
+#pragma unroll
+        for (int i = 0; i < NH; i += 4) *reinterpret_cast<float4*>(dst + i) = make_float4(v[i], v[i + 1], v[i + 2], v[i + 3]);
+      }
+      __threadfence();
+      named_bar_sync(2, 32 * kEpiWarps);
+      if (et == 0) last_flag = (!dead && atomicAdd(&cnt[tile], 1) == sp.n_dblk - 1) ? 1 : 0;
+      named_bar_sync(2, 32 * kEpiWarps);
+      if (last_flag && lane < 16) {
+        __threadfence();
+        float acc[NH];
+#pragma unroll
+        for (int i = 0; i < NH; ++i) acc[i] = 0.f;
+        for (int k2 = 0; k2 < sp.n_dblk; ++k2) {
+          const float* src = dzp + (((size_t)k2 * sp.n_tiles + tile) * kBT + tok) * RKP + c0;
+#pragma unroll
+          for (int i = 0; i < NH; i += 4) {
+            const float4 f = __ldcg(reinterpret_cast<const float4*>(src + i));
+            acc[i] += f.x;
+            acc[i + 1] += f.y;
+            acc[i + 2] += f.z;
+            acc[i + 3] += f.w;
+          }
+        }
+        const int t = t0 + tok;
+        if (t < T) {
+          __nv_bfloat16* dst = dz + ((size_t)b * T + t) * R;
+#pragma unroll
+          for (int i = 0; i < NH; ++i)
+            if (c0 + i < R) dst[c0 + i] = __float2bfloat16_rn(acc[i]);
+        }
+      }
+    };
+
+    for (int k = 0; k < n; ++k) {
+      const int s = k % kBwdStages, p = k % NP;
+      const int tile = j0 + k, b = tile / sp.tiles_row, t0 = (tile % sp.tiles_row) * kBT;
+      if (!dead) dead = !mbar_wait(&full_bar[s], (k / kBwdStages) & 1, kErrWaitEpilogue, &abort_flag);
+      if (!dead) dead = !mbar_wait(&pe_bar[p], ((k / NP) & 1) ^ 1, kErrWaitEpilogue, &abort_flag);
+      const __nv_bfloat16* dys = reinterpret_cast<const __nv_bfloat16*>(smem + L::kOffDy + s * L::kTileStride);
+      const __nv_bfloat16* xs = reinterpret_cast<const __nv_bfloat16*>(smem + L::kOffX + s * L::kTileStride);
+      uint8_t* pbuf = smem + L::kOffP + p * W * L::kPTap;
+#pragma unroll
+      for (int h = 0; h < 2; ++h) {
+        if (!dead) dead = !mbar_wait(&a1f_bar[h], k & 1, kErrWaitEpilogue, &abort_flag);
+        tc_fence_after();
+        if (!dead) {
+          const int tb = 32 * h + 16 * pp;
+          float acc[W][16];
+#pragma unroll
+          for (int w = 0; w < W; ++w) tmem_ld16(tmem + lane_base + L::kColA1 + h * 32 * W + w * 32 + 16 * pp, acc[w]);
+          float dyr[16 + W - 1], xr[16 + W - 1];
+#pragma unroll
+          for (int j = 0; j < 16 + W - 1; ++j) {
+            dyr[j] = __bfloat162float(dys[(tb + j) * kBD + ch]);  // dy at step tb + j
+            xr[j] = __bfloat162float(xs[(tb + j) * kBD + ch]);    // x at step tb - (W-1) + j
+          }
+          tmem_ld_wait();
+          __nv_bfloat16* dxc = dx + ((size_t)b * T + t0 + tb) * D + d0 + ch;
+#pragma unroll
+          for (int j = 0; j < 16; ++j) {
+            float v = 0.f;
+#pragma unroll
+            for (int w = 0; w < W; ++w) v = fmaf(acc[w][j], dyr[j + w], v);
+            if (residual) v += dyr[j];
+            if (dok && t0 + tb + j < T) dxc[(size_t)j * D] = __float2bfloat16_rn(v);
+          }
+#pragma unroll
+          for (int w = 0; w < W; ++w) {
+#pragma unroll
+            for (int hh = 0; hh < 2; ++hh) {
+              __align__(16) __nv_bfloat162 pk[4];
+#pragma unroll
+              for (int i = 0; i < 4; ++i) {
+                const int j = 8 * hh + 2 * i;
+                pk[i] = __floats2bfloat162_rn(dyr[j] * xr[j + W - 1 - w], dyr[j + 1] * xr[j + W - w]);
+              }
+              *reinterpret_cast<uint4*>(pbuf + w * L::kPTap + kmajor_off(ch, tb + 8 * hh, L::kPChunk, 128)) =
+                  *reinterpret_cast<uint4*>(pk);
+            }
+          }
+        }
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&a1e_bar[h]);
+      }
+      fence_proxy_async_smem();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&pf_bar[p]);
+      if (k >= 1) dz_readout(k - 1);
+    }
+    if (n >= 1) dz_readout(n - 1);
+    // dU partial of this CTA: TMEM (lane = channel) -> dUp[g][r][w*D + d0 + ch]
+    if (!dead) dead = !mbar_wait(&du_bar, 0, kErrWaitTail, &abort_flag);
+    tc_fence_after();
+    if (!dead && pp == 0) {
+#pragma unroll
+      for (int w = 0; w < W; ++w) {
+#pragma unroll
+        for (int rc = 0; rc < RKP / 16; ++rc) {
+          float v[16];
+          tmem_ld16(tmem + lane_base + L::kColDU + w * RKP + rc * 16, v);
+          tmem_ld_wait();
+#pragma unroll
+          for (int i = 0; i < 16; ++i) {
+            const int r = rc * 16 + i;
+            if (r < Rk && dok) dUp[((size_t)g * Rk + r) * W * D + (size_t)w * D + d0 + ch] = v[i];
+          }
+        }
+      }
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) tmem_dealloc(tmem, L::kAlloc);
+}
+
+struct BwdWorkspace {
+  float* dzp;
+  int* cnt;
+  float* dUp;
+  void* zp;
+  size_t bytes;
+};
+
+static size_t al256(size_t v) { return (v + 255) / 256 * 256; }
+
+BwdWorkspace bwd_workspace(void* base, int64_t B, int64_t T, int64_t D, int Rk, int W) {
+  const TileSplit sp = tile_split(B, T, D);
+  const int rkp = Rk <= 16 ? 16 : 32;
+  BwdWorkspace w;
+  const size_t dzp = al256((size_t)sp.n_dblk * sp.n_tiles * kBT * rkp * sizeof(float));
+  const size_t cnt = al256((size_t)sp.n_tiles * sizeof(int));
+  const size_t dUp = al256((size_t)sp.n_groups * Rk * W * D * sizeof(float));
+  const size_t zp = zpack_bytes(B, T, rkp);
+  uint8_t* p = (uint8_t*)base;
+  w.dzp = (float*)p;
+  w.cnt = (int*)(p ? p + dzp : nullptr);
+  w.dUp = (float*)(p ? p + dzp + cnt : nullptr);
+  w.zp = p ? p + dzp + cnt + dUp : nullptr;
+  w.bytes = dzp + cnt + dUp + zp;
+  return w;
+}
+
+template <int W, int RKP>
+int launch_bwd(const void* x, const void* z, const void* U, const void* sw, const void* dy, void* dx, void* dz,
+               float* dU_f32, void* dU, void* dsw, void* wsp, int64_t B, int64_t T, int64_t D, int R, int Rk,
+               int residual, cudaStream_t st) {
+  constexpr int NP = RKP == 16 ? 2 : 1;
+  using L = BwdSmem<W, RKP, NP>;
+  static_assert(L::kTotal <= 232448 - 512, "backward shared memory budget (227 KB per CTA)");
+  CUtensorMap dymap, xmap, zmap;
+  int s;
+  const TileSplit sp = tile_split(B, T, D);
+  BwdWorkspace ws = bwd_workspace(wsp, B, T, D, Rk, W);
+  if ((s = make_btd_map(&dymap, dy, B, T, D, kBD, kBT + W - 1))) return s;
+  if ((s = make_btd_map(&xmap, x, B, T, D, kBD, kBT + W - 1))) return s;
+  if ((s = make_zpack_map(&zmap, ws.zp, B, T, RKP, kZRows))) return s;
+  if ((s = z_pack_launch(z, ws.zp, B, T, R, RKP, sw != nullptr, st))) return s;
+  cudaError_t e = cudaMemsetAsync(ws.cnt, 0, (size_t)sp.n_tiles * sizeof(int), st);
+  if (e != cudaSuccess) return cuda_status(e, "cudaMemsetAsync(tile counters)");
+  const int smem = (int)L::kTotal;
+  e = cudaFuncSetAttribute(lr_bwd_tc_kernel<W, RKP, NP>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+  if (e != cudaSuccess) {
+    cudaGetLastError();
+    return cuda_status(e, "cudaFuncSetAttribute(lr_bwd_tc)");
+  }
+  lr_bwd_tc_kernel<W, RKP, NP><<<sp.n_dblk * sp.n_groups, kBwdThreads, smem, st>>>(
+      dymap, xmap, zmap, (const __nv_bfloat16*)U, (const __nv_bfloat16*)sw, (__nv_bfloat16*)dx, (__nv_bfloat16*)dz,
+      ws.dzp, ws.cnt, ws.dUp, sp, (int)T, (int)D, R, Rk, residual);
+  DYNCONV_CHECK_LAUNCH("lr_bwd_tc_kernel");
+  const int64_t nacc = (int64_t)Rk * W * D;
+  if ((s = reduce_partials_launch(ws.dUp, sp.n_groups, nacc, dU_f32, nullptr, DYNCONV_DTYPE_BF16, st))) return s;
+  if (dU && (s = cast_f32_launch(dU_f32, dU, (int64_t)R * W * D, DYNCONV_DTYPE_BF16, st))) return s;
+  if (sw && dsw && (s = cast_f32_launch(dU_f32 + (int64_t)R * W * D, dsw, (int64_t)W * D, DYNCONV_DTYPE_BF16, st)))
+    return s;
+  return DYNCONV_OK;
+}
+
+template <int RKP>
+int launch_bwd_w(int W, const void* x, const void* z, const void* U, const void* sw, const void* dy, void* dx,
+                 void* dz, float* dU_f32, void* dU, void* dsw, void* ws, int64_t B, int64_t T, int64_t D, int R,
+                 int Rk, int residual, cudaStream_t st) {
+  switch (W) {
+    case 1: return launch_bwd<1, RKP>(x, z, U, sw, dy, dx, dz, dU_f32, dU, dsw, ws, B, T, D, R, Rk, residual, st);
+    case 2: return launch_bwd<2, RKP>(x, z, U, sw, dy, dx, dz, dU_f32, dU, dsw, ws, B, T, D, R, Rk, residual, st);
+    case 3: return launch_bwd<3, RKP>(x, z, U, sw, dy, dx, dz, dU_f32, dU, dsw, ws, B, T, D, R, Rk, residual, st);
+    case 4: return launch_bwd<4, RKP>(x, z, U, sw, dy, dx, dz, dU_f32, dU, dsw, ws, B, T, D, R, Rk, residual, st);
+    default: return set_error(DYNCONV_ERR_UNSUPPORTED, "tensor-core backward: W=%d", W);
   }
 }
 
@@ -372,8 +834,10 @@ bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 
 // pitch), 16-byte aligned activations (TMA base).  Everything else runs the
 // CUDA-core kernels of lowrank_simple.cu.
 bool lr_tc_bwd_supported(int64_t D, int Rk, int W, int dtype, const void* const* ptrs, int nptrs) {
-  (void)D; (void)Rk; (void)W; (void)dtype; (void)ptrs; (void)nptrs;
-  return false;
+  if (dtype != DYNCONV_DTYPE_BF16 || W < 1 || W > 4 || Rk < 1 || Rk > 32 || D % 8 != 0) return false;
+  for (int i = 0; i < nptrs; ++i)
+    if (ptrs[i] && !aligned16(ptrs[i])) return false;
+  return encode_fn() != nullptr || nptrs == 0;
 }
 
 bool lr_tc_supported(int64_t D, int Rk, int W, int dtype, const void* const* ptrs, int nptrs) {
@@ -384,25 +848,32 @@ bool lr_tc_supported(int64_t D, int Rk, int W, int dtype, const void* const* ptr
 }
 
 size_t lr_tc_bwd_workspace(int64_t B, int64_t T, int64_t D, int Rk, int W) {
-  (void)B; (void)T; (void)D; (void)Rk; (void)W;
-  return 0;
+  return bwd_workspace(nullptr, B, T, D, Rk, W).bytes;
 }
 
-int lr_tc_fwd_launch(const void* x, const void* z, const void* U, const void* sw, void* y, int64_t B, int64_t T,
-                     int64_t D, int R, int Rk, int W, int residual, cudaStream_t st) {
+size_t lr_tc_fwd_workspace(int64_t B, int64_t T, int Rk) { return zpack_bytes(B, T, (Rk + 15) / 16 * 16); }
+
+int lr_tc_fwd_launch(const void* x, const void* z, const void* U, const void* sw, void* y, void* ws, size_t ws_bytes,
+                     int64_t B, int64_t T, int64_t D, int R, int Rk, int W, int residual, cudaStream_t st) {
+  if (!ws || ws_bytes < lr_tc_fwd_workspace(B, T, Rk))
+    return set_error(DYNCONV_ERR_WORKSPACE, "lr_fwd (tensor core): workspace too small");
   const int rkp = (Rk + 15) / 16 * 16;
   switch (rkp) {
-    case 16: return launch_fwd_w<16>(W, x, z, U, sw, y, B, T, D, R, residual, st);
-    case 32: return launch_fwd_w<32>(W, x, z, U, sw, y, B, T, D, R, residual, st);
-    case 48: return launch_fwd_w<48>(W, x, z, U, sw, y, B, T, D, R, residual, st);
-    case 64: return launch_fwd_w<64>(W, x, z, U, sw, y, B, T, D, R, residual, st);
+    case 16: return launch_fwd_w<16>(W, x, z, U, sw, y, ws, B, T, D, R, residual, st);
+    case 32: return launch_fwd_w<32>(W, x, z, U, sw, y, ws, B, T, D, R, residual, st);
+    case 48: return launch_fwd_w<48>(W, x, z, U, sw, y, ws, B, T, D, R, residual, st);
+    case 64: return launch_fwd_w<64>(W, x, z, U, sw, y, ws, B, T, D, R, residual, st);
     default: return set_error(DYNCONV_ERR_UNSUPPORTED, "R_kernel=%d", Rk);
   }
 }
 
-int lr_tc_bwd_launch(const void*, const void*, const void*, const void*, const void*, void*, void*, float*, void*,
-                     void*, void*, size_t, int64_t, int64_t, int64_t, int, int, int, int, cudaStream_t) {
-  return set_error(DYNCONV_ERR_UNSUPPORTED, "tensor-core lowrank backward not built");
+int lr_tc_bwd_launch(const void* x, const void* z, const void* U, const void* sw, const void* dy, void* dx, void* dz,
+                     float* dU_f32, void* dU, void* dsw, void* ws, size_t ws_bytes, int64_t B, int64_t T, int64_t D,
+                     int R, int Rk, int W, int residual, cudaStream_t st) {
+  if (ws_bytes < lr_tc_bwd_workspace(B, T, D, Rk, W))
+    return set_error(DYNCONV_ERR_WORKSPACE, "lr_bwd (tensor core): workspace too small");
+  if (Rk <= 16) return launch_bwd_w<16>(W, x, z, U, sw, dy, dx, dz, dU_f32, dU, dsw, ws, B, T, D, R, Rk, residual, st);
+  return launch_bwd_w<32>(W, x, z, U, sw, dy, dx, dz, dU_f32, dU, dsw, ws, B, T, D, R, Rk, residual, st);
 }
 
 }  // namespace dynconv

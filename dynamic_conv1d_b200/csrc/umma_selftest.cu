@@ -23,10 +23,13 @@ __global__ void __launch_bounds__(128) umma_selftest_kernel(const __nv_bfloat16*
   uint8_t* Bs = smem + a_bytes;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
 
-  for (int i = tid; i < M * K; i += blockDim.x) {
-    const int m = i / K, k = i % K;
-    const uint32_t off = a_major ? mnmajor_off(m, k, a_sbo, a_lbo) : kmajor_off(m, k, a_sbo, a_lbo);
-    *reinterpret_cast<__nv_bfloat16*>(As + off) = A[i];
+  const bool a_tmem = (a_major == 2);  // A staged in TMEM after the D columns
+  if (!a_tmem) {
+    for (int i = tid; i < M * K; i += blockDim.x) {
+      const int m = i / K, k = i % K;
+      const uint32_t off = a_major ? mnmajor_off(m, k, a_sbo, a_lbo) : kmajor_off(m, k, a_sbo, a_lbo);
+      *reinterpret_cast<__nv_bfloat16*>(As + off) = A[i];
+    }
   }
   for (int i = tid; i < K * Nb; i += blockDim.x) {
     const int k = i / Nb, n = i % Nb;
@@ -47,14 +50,36 @@ __global__ void __launch_bounds__(128) umma_selftest_kernel(const __nv_bfloat16*
   __syncthreads();
   tc_fence_after();
   const uint32_t tbase = tmem_slot;
+  const uint32_t a_col = (uint32_t)N;  // A columns follow the N accumulator columns
+  if (a_tmem) {
+    // M == 128: warp w writes rows 32w..32w+31, K/2 packed columns per row, 8 at a time
+    const int m = 32 * warp + lane;
+    for (int c0 = 0; c0 < K / 2; c0 += 8) {
+      uint32_t v[8];
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        const __nv_bfloat162 p2 = __halves2bfloat162(A[(size_t)m * K + 2 * (c0 + j)], A[(size_t)m * K + 2 * (c0 + j) + 1]);
+        v[j] = *reinterpret_cast<const uint32_t*>(&p2);
+      }
+      tmem_st8(tbase + ((uint32_t)(32 * warp) << 16) + a_col + (uint32_t)c0, v);
+    }
+    tmem_st_wait();
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+  }
 
   if (tid == 0) {
-    const uint32_t idesc = make_idesc_bf16(M, N, a_major, b_major);
+    const uint32_t idesc = make_idesc_bf16(M, N, a_tmem ? 0 : a_major, b_major);
     const uint32_t a0 = smem_u32(As), b0 = smem_u32(Bs) + (uint32_t)b_off * 16u;
     for (int ks = 0; ks < K / 16; ++ks) {
-      const uint64_t ad = make_smem_desc(a0 + (uint32_t)ks * 2u * a_lbo, a_lbo, a_sbo);
       const uint64_t bd = make_smem_desc(b0 + (uint32_t)ks * 2u * b_lbo, b_lbo, b_sbo);
-      umma_f16(tbase, ad, bd, idesc, ks > 0 ? 1u : 0u);
+      if (a_tmem) {
+        umma_f16_ts(tbase, tbase + a_col + (uint32_t)ks * 8u, bd, idesc, ks > 0 ? 1u : 0u);
+      } else {
+        const uint64_t ad = make_smem_desc(a0 + (uint32_t)ks * 2u * a_lbo, a_lbo, a_sbo);
+        umma_f16(tbase, ad, bd, idesc, ks > 0 ? 1u : 0u);
+      }
     }
     umma_commit(&bar);
   }
@@ -96,12 +121,14 @@ int umma_selftest_launch(const void* A, const void* B, float* D, int M, int N, i
   if (b_off != 0 && (b_major != 0 || b_sbo != 128))
     return set_error(DYNCONV_ERR_SHAPE, "selftest: row offset needs K-major B with SBO = 128");
   if ((a_sbo | a_lbo | b_sbo | b_lbo) & 15) return set_error(DYNCONV_ERR_ALIGN, "selftest: strides must be 16-byte multiples");
-  const uint32_t abytes = span_bytes(a_major, M, K, (uint32_t)a_sbo, (uint32_t)a_lbo);
+  if (a_major == 2 && (M != 128 || N + K / 2 > 256))
+    return set_error(DYNCONV_ERR_SHAPE, "selftest: A in TMEM needs M = 128 and N + K/2 <= 256");
+  const uint32_t abytes = a_major == 2 ? 128u : span_bytes(a_major, M, K, (uint32_t)a_sbo, (uint32_t)a_lbo);
   const uint32_t bbytes = span_bytes(b_major, Nb, K, (uint32_t)b_sbo, (uint32_t)b_lbo);
   const uint32_t smem = abytes + bbytes;
   if (smem > 200 * 1024) return set_error(DYNCONV_ERR_SHAPE, "selftest: operands need %u bytes of smem", smem);
   uint32_t ncols = 32;
-  while (ncols < (uint32_t)N) ncols <<= 1;
+  while (ncols < (uint32_t)N + (a_major == 2 ? (uint32_t)K / 2 : 0u)) ncols <<= 1;
   // Reserve the whole shared memory so any descriptor walk stays inside this CTA's window.
   const int smem_alloc = 220 * 1024;
   cudaError_t e = cudaFuncSetAttribute(umma_selftest_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem_alloc);

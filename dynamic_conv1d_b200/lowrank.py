@@ -6,9 +6,11 @@ meaning and the same ``assert`` preconditions as the reference
 (``lowrank.py:214-338``).  Differences that a caller can observe only as
 "more general" or "less memory traffic":
 
-* the static filter is folded in as rank R inside the kernels; nothing is
-  padded or concatenated in HBM (the reference builds ``F.pad(z)`` and
-  ``torch.cat([U, static_w])``, lowrank.py:222-226);
+* the static filter is folded in as rank R inside the kernels; ``U`` is never
+  concatenated with ``static_w`` (the reference builds ``F.pad(z)`` and
+  ``torch.cat([U, static_w])``, lowrank.py:222-226); on the bf16 tensor-core path
+  ``z`` plus the static rank is packed once per call into a small workspace in the
+  layout the TMA unit places directly into the MMA operand;
 * the returned ``dz`` / ``dU`` are dense tensors of the caller's shapes (the
   reference returns slices of padded buffers, lowrank.py:295-299);
 * the dU / dstatic_w reduction is deterministic (fixed-order two-pass; the
@@ -38,9 +40,12 @@ class _LowrankDynamicConvolutionFn(torch.autograd.Function):
         U_k = U if U.dtype == x.dtype else U.to(x.dtype)
         sw_k = static_w if (static_w is None or static_w.dtype == x.dtype) else static_w.to(x.dtype)
         y = torch.empty_like(x)
+        nbytes = lib.dynconv_lr_fwd_workspace_bytes(B, T, D, R, W, code, int(static_w is not None))
+        ws = torch.empty(max(int(nbytes), 1), device=x.device, dtype=torch.uint8)
         _lib.check(
             lib.dynconv_lr_fwd(
                 _lib.ptr(x), _lib.ptr(z_k), _lib.ptr(U_k), _lib.ptr(sw_k), _lib.ptr(y),
+                _lib.ptr(ws), ws.numel(),
                 B, T, D, R, W, code, int(bool(residual)), _lib.stream_of(x),
             )
         )

@@ -91,13 +91,20 @@ int dynconv_hw_bwd(const void* x, const void* weight, const void* static_w, cons
 
 /* ----------------------------------------------------------------- lowrank */
 
+/* Workspace for dynconv_lr_fwd (bytes; may be 0). */
+size_t dynconv_lr_fwd_workspace_bytes(int64_t B, int64_t T, int64_t D, int64_t R, int64_t W,
+                                      int dtype, int has_static);
+
 /* y = sum_w ((z@U).view(B,T,W,D)[b,t,w,d] + static_w[w,d]) * x[b,t-w,d] (+ x)
  * Replaces the static-rank fold (F.pad / torch.cat, lowrank.py:222-226) and the
  * causal_conv1d_fwd_kernel launch (lowrank.py:230-242) of
- * _LowrankDynamicConvolutionFn.forward.  static_w is folded in on chip as rank R
- * (R_kernel = R + 1); nothing is padded or concatenated in HBM.  Any R >= 1 with
- * R_kernel <= 64 is accepted (the reference needs R_kernel a power of two >= 16). */
+ * _LowrankDynamicConvolutionFn.forward.  static_w is folded in as rank R
+ * (R_kernel = R + 1); U is never concatenated.  The bf16 tensor-core path packs
+ * z_ext (z plus the static rank) into the workspace, [R_kernel/8][B][T][8], so
+ * TMA can place it in the MMA operand layout.  Any R >= 1 with R_kernel <= 64 is
+ * accepted (the reference needs R_kernel a power of two >= 16). */
 int dynconv_lr_fwd(const void* x, const void* z, const void* U, const void* static_w, void* y,
+                   void* workspace, size_t workspace_bytes,
                    int64_t B, int64_t T, int64_t D, int64_t R, int64_t W,
                    int dtype, int residual, void* stream);
 
@@ -131,8 +138,9 @@ int dynconv_cast_f32(const float* src, void* dst, int64_t n, int dtype, void* st
  * lowrank kernels, for the unit tests of descriptor encodings.  No reference
  * counterpart.  A: logical [M][K] bf16 row-major; B: logical [K][Nb] bf16
  * row-major (Nb >= N + b_row_offset); D: [M][N] float32 = A @ B[:, off:off+N].
- * a_major/b_major: 0 = K-major, 1 = MN-major; *_sbo/*_lbo: byte strides of the
- * staged layout; b_row_offset shifts a K-major B by whole rows (16 B each). */
+ * a_major/b_major: 0 = K-major, 1 = MN-major (a_major 2: A staged K-major in
+ * tensor memory, M = 128); *_sbo/*_lbo: byte strides of the staged layout;
+ * b_row_offset shifts a K-major B by whole rows (16 B each). */
 int dynconv_umma_selftest(const void* A, const void* B, float* D,
                           int M, int N, int K, int Nb,
                           int a_major, int a_sbo, int a_lbo,

@@ -164,6 +164,11 @@ EDGE = [
     ("lowrank", 1, 129, 136, 63, 4, True, False),   # R_kernel = 64, D not a multiple of 128
     ("lowrank", 1, 70, 128, 15, 8, True, True),     # W = 8
     ("lowrank", 2, 64, 128, 1, 4, False, True),     # R = 1
+    # several 64-step tiles per persistent CTA (pipeline wrap-around, dz ticket reuse)
+    ("lowrank", 2, 2048, 1024, 15, 4, True, True),
+    ("lowrank", 1, 8192, 512, 31, 4, True, True),   # R_kernel = 32
+    ("lowrank", 3, 3000, 384, 15, 3, True, True),   # W = 3, ragged T
+    ("headwise", 2, 2048, 1024, 32, 4, True, True),
 ]
 
 

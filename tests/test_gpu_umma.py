@@ -31,6 +31,12 @@ CASES = {
     "dz_R32": (64, 32, 128, 32, 1, 128, 1024, 1, 128, 512, 0),
     # wide N, two K steps
     "wide": (128, 256, 32, 256, 0, 512, 128, 0, 512, 128, 0),
+    # A operand in tensor memory (a_major = 2): weight MMAs (A = U) and the dU MMA (A = P^T)
+    "tmemA_fwd_R16": (128, 64, 16, 64, 2, 0, 0, 0, 128, 64 * 16, 0),
+    "tmemA_fwd_R32": (128, 64, 32, 64, 2, 0, 0, 0, 128, 64 * 16, 0),
+    "tmemA_dx_shift2": (128, 32, 16, 72, 2, 0, 0, 0, 128, 72 * 16, 2),
+    "tmemA_dU_R16": (128, 16, 64, 16, 2, 0, 0, 1, 72 * 16, 128, 0),
+    "tmemA_dU_R32": (128, 32, 64, 32, 2, 0, 0, 1, 72 * 16, 128, 0),
 }
 
 

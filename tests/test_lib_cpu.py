@@ -62,7 +62,7 @@ def test_validation_without_gpu():
     assert _hw_fwd() == 7  # null tensors
     assert b"null" in lib.dynconv_last_error()
     # lowrank: R_kernel > 64 and missing accumulator
-    st = lib.dynconv_lr_fwd(None, None, None, None, None, 1, 4, 16, 65, 4, 0, 0, None)
+    st = lib.dynconv_lr_fwd(None, None, None, None, None, None, 0, 1, 4, 16, 65, 4, 0, 0, None)
     assert st == 3
     st = lib.dynconv_lr_bwd(*([None] * 10), None, 0, 1, 4, 16, 15, 4, 0, 0, None)
     assert st == 7
