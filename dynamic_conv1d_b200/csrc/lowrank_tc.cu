@@ -403,26 +403,41 @@ int launch_fwd_w(int W, const void* x, const void* z, const void* U, const void*
 // One fused pass over dy and x per work item (128 channels x 64 timesteps):
 //
 //   MMA-1  acc1_w[ch][t] = sum_r U[r,w,ch] z[t+w,r]    M=128 ch, N=32 t (two halves), K=R_kernel
-//          (B = the z tile read from row w: the no-swizzle K-major layout is linear in rows)
+//          A = U^T held in TMEM for the whole kernel; B = the z tile read from row w
+//          (the no-swizzle K-major layout is linear in rows).
 //   epilogue: dx[t,ch] = sum_w acc1_w[ch][t] dy[t+w,ch] (+ dy)   -> HBM (bf16)
-//             P_w[t,ch] = bf16(dy[t,ch] x[t-w,ch])               -> smem (bf16, as the
-//             reference rounds dy*x to bf16 before its dots, lowrank.py:128)
+//             P_w[t,ch] = bf16(dy[t,ch] x[t-w,ch])   (rounded to bf16 as the reference
+//             does before its dots, lowrank.py:128) -> smem, and transposed -> TMEM
 //   MMA-2  dU_w[ch][r] += sum_t P_w[t,ch] z[t,r]       M=128 ch, N=R_kernel, K=64 t
-//          (accumulated in TMEM over all items of the CTA; one partial row block per CTA)
+//          A = P^T from TMEM (R_kernel <= 16; else from smem), B = z (MN-major view);
+//          accumulated in TMEM over all items of the CTA, one partial block per CTA.
 //   MMA-3  dz[t][r]     = sum_{w,ch} P_w[t,ch] U[r,w,ch] M=64 t,  N=R_kernel, K=128*W
-//          (partial over this CTA's 128 channels; the last of the channel-block CTAs
-//          of a tile, by an atomic ticket, sums the partials in channel-block order)
+//          A = P (smem, MN-major view), B = U (smem); partial over this CTA's 128
+//          channels, written to the workspace.  After its last tile every CTA of a
+//          token group publishes its partials (one fence + counter), waits for the
+//          group's other channel-block CTAs (co-resident: cooperative launch) and
+//          sums a 1/n_dblk slice of the group's dz in channel-block order:
+//          deterministic, and the reduction work is spread evenly.
 //
-// The P buffer serves MMA-2 as a K-major A operand and MMA-3 as an MN-major A
-// operand; the z tile serves MMA-1 (K-major B) and MMA-2 (MN-major B); the U
-// block serves MMA-1 (K-major A) and MMA-3 (MN-major B): one smem copy each.
+// Why operands live where they do: one tcgen05.mma costs about one pass of its
+// shared-memory operands at ~128 B/clock (a 128x16 bf16 A operand alone is 4 KB),
+// so the A operands that are either constant (U) or produced lane-per-channel by
+// the epilogue (P^T) are kept in TMEM and only the small B operands are read from
+// shared memory.  MMA-3 needs P with timesteps as rows, so it reads P from shared
+// memory; it runs on its own issuing warp (M = 64 MMAs from two issuers overlap).
+//
+// Warps: 0 producer (TMA), 1 MMA-1/MMA-2 issuer + TMEM owner, 2 MMA-3 issuer,
+// 3..18 epilogue (four per TMEM lane quarter, one per 8-step piece of each half).
 // Grid = n_dblk x n_groups CTAs: CTA (dblk, g) owns channel block dblk for a
 // contiguous range of 64-step tiles, so the CTAs sharing a tile's dz run in step
 // and the dz partial working set stays small and L2-resident.
 
 constexpr int kBwdStages = 2;
 constexpr int kZRows = 72;  // z rows t0 .. t0+71 (64 + W-1 look-ahead, rounded up to whole core matrices)
-constexpr int kBwdThreads = 64 + 32 * kEpiWarps;
+constexpr int kBwdCtl = 3;       // control warps
+constexpr int kBwdEpi = 16;      // epilogue warps
+constexpr int kBwdPiece = 8;     // timesteps per epilogue warp and half
+constexpr int kBwdThreads = 32 * (kBwdCtl + kBwdEpi);
 
 __host__ __device__ constexpr uint32_t round1024(uint32_t v) { return (v + 1023u) / 1024u * 1024u; }
 
@@ -446,9 +461,12 @@ struct BwdSmem {
   static constexpr uint32_t kZChunk = kZRows * 16;      // z: next 8 ranks
   static constexpr uint32_t kPChunk = (kBT / 8) * 128;  // P: next 8 channels
   // TMEM columns
-  static constexpr uint32_t kColA1 = 0;                       // 2 halves x W taps x 32
-  static constexpr uint32_t kColDU = 64 * W;                  // W x RKP
-  static constexpr uint32_t kColDZ = kColDU + W * RKP;        // 2 x RKP
+  static constexpr bool kPT = (RKP == 16);                  // P^T for MMA-2 held in TMEM
+  static constexpr uint32_t kColA1 = 0;                     // 2 halves x W taps x 32 steps
+  static constexpr uint32_t kColUA = 64 * W;                // U^T: W taps x RKP/2 (bf16 pairs)
+  static constexpr uint32_t kColPT = kColUA + W * RKP / 2;  // P^T: W taps x 32 (64 steps, bf16 pairs)
+  static constexpr uint32_t kColDU = kColPT + (kPT ? 32 * W : 0);
+  static constexpr uint32_t kColDZ = kColDU + W * RKP;      // 2 x RKP, M = 64 layout
   static constexpr uint32_t kCols = kColDZ + 2 * RKP;
   static constexpr uint32_t kAlloc = kCols <= 256 ? 256 : 512;
   static_assert(kCols <= 512, "TMEM budget");
@@ -456,9 +474,15 @@ struct BwdSmem {
 
 template <int N>
 __device__ __forceinline__ void tmem_ld_n(uint32_t taddr, float (&v)[N]) {
-  static_assert(N == 8 || N == 16, "");
-  if constexpr (N == 8) tmem_ld8(taddr, v);
+  static_assert(N == 4 || N == 8 || N == 16, "");
+  if constexpr (N == 4) tmem_ld4(taddr, v);
+  else if constexpr (N == 8) tmem_ld8(taddr, v);
   else tmem_ld16(taddr, v);
+}
+
+__device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
+  const __nv_bfloat162 p = __floats2bfloat162_rn(lo, hi);
+  return *reinterpret_cast<const uint32_t*>(&p);
 }
 
 template <int W, int RKP, int NP>
@@ -466,16 +490,16 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
     lr_bwd_tc_kernel(const __grid_constant__ CUtensorMap dymap, const __grid_constant__ CUtensorMap xmap,
                      const __grid_constant__ CUtensorMap zmap, const __nv_bfloat16* __restrict__ U,
                      const __nv_bfloat16* __restrict__ sw, __nv_bfloat16* __restrict__ dx,
-                     __nv_bfloat16* __restrict__ dz, float* __restrict__ dzp, int* __restrict__ cnt,
+                     __nv_bfloat16* __restrict__ dz, float* __restrict__ dzp, int* __restrict__ grp_done,
                      float* __restrict__ dUp, TileSplit sp, int T, int D, int R, int Rk, int residual) {
   using L = BwdSmem<W, RKP, NP>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = align_smem_1024(smem_raw);
   __shared__ uint64_t full_bar[kBwdStages], empty_bar[kBwdStages], a1f_bar[2], a1e_bar[2], pf_bar[NP], pe_bar[NP],
-      dzf_bar[2], dze_bar[2], du_bar;
+      pte_bar, dzf_bar[2], dze_bar[2], du_bar;
   __shared__ uint32_t tmem_slot;
   __shared__ int abort_flag;
-  __shared__ volatile int last_flag;
+  __shared__ int grp_ok;
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int dblk = blockIdx.x % sp.n_dblk;
@@ -493,17 +517,17 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
     }
     for (int h = 0; h < 2; ++h) {
       mbar_init(&a1f_bar[h], 1);
-      mbar_init(&a1e_bar[h], kEpiWarps);
+      mbar_init(&a1e_bar[h], kBwdEpi);
       mbar_init(&dzf_bar[h], 1);
-      mbar_init(&dze_bar[h], kEpiWarps);
+      mbar_init(&dze_bar[h], kBwdEpi);
     }
     for (int p = 0; p < NP; ++p) {
-      mbar_init(&pf_bar[p], kEpiWarps);
-      mbar_init(&pe_bar[p], 1);
+      mbar_init(&pf_bar[p], kBwdEpi);
+      mbar_init(&pe_bar[p], L::kPT ? 1 : 2);  // MMA-3 (and MMA-2 when it reads P from smem)
     }
+    mbar_init(&pte_bar, 1);
     mbar_init(&du_bar, 1);
     abort_flag = 0;
-    last_flag = 0;
     fence_barrier_init();
   }
   if (warp == 0 && lane == 0) {
@@ -511,7 +535,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
     prefetch_tensormap(&xmap);
     prefetch_tensormap(&zmap);
   }
-  // U block of this CTA's channels (MMA-1 A operand, MMA-3 B operand), loaded once.
+  // U block of this CTA's channels in smem (MMA-3 B operand), loaded once.
   load_u_block<W, RKP>(smem + L::kOffU, U, sw, dblk, D, R, threadIdx.x, blockDim.x);
   fence_proxy_async_smem();
   if (warp == 1) {
@@ -522,10 +546,40 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = tmem_slot;
+  // U^T in TMEM (MMA-1 A operand): lane = channel, column c of tap w = ranks (2c, 2c+1).
+  if (warp >= kBwdCtl && ((warp - kBwdCtl) >> 2) == 0) {  // one warp per lane quarter
+    const int q = warp & 3, ch = q * 32 + lane, d = d0 + ch;
+#pragma unroll
+    for (int w = 0; w < W; ++w) {
+#pragma unroll
+      for (int c0 = 0; c0 < RKP / 2; c0 += 8) {
+        uint32_t v[8];
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+          float f[2];
+#pragma unroll
+          for (int k2 = 0; k2 < 2; ++k2) {
+            const int r = 2 * (c0 + i) + k2;
+            f[k2] = 0.f;
+            if (d < D) {
+              if (r < R) f[k2] = __bfloat162float(U[((size_t)r * W + w) * D + d]);
+              else if (r == R && has_static) f[k2] = __bfloat162float(sw[(size_t)w * D + d]);
+            }
+          }
+          v[i] = pack_bf16x2(f[0], f[1]);
+        }
+        tmem_st8(tmem + ((uint32_t)(q * 32) << 16) + L::kColUA + w * (RKP / 2) + c0, v);
+      }
+    }
+    tmem_st_wait();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
 
   if (warp == 0) {
     // ------------------------------------------------------------ producer
-    // Stage k % 2 is released by the commit after the MMAs of tile k-2.
+    // Stage k % 2 is released by the commit after the MMAs of tile k-2 that read it.
     if (lane == 0) {
       const uint64_t pol = policy_evict_first();
       for (int k = 0; k < n; ++k) {
@@ -540,41 +594,33 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
     }
     __syncwarp();
   } else if (warp == 1) {
-    // ------------------------------------------------------------ MMA issuer
-    uint8_t* us = smem + L::kOffU;
-    const uint32_t ub = smem_u32(us), pb0 = smem_u32(smem + L::kOffP);
+    // ------------------------------------------------------------ MMA-1 / MMA-2 issuer
+    const uint32_t pb0 = smem_u32(smem + L::kOffP);
     const uint32_t idesc1 = make_idesc_bf16(kBD, 32, 0, 0);
     const uint32_t idesc2 = make_idesc_bf16(kBD, RKP, 0, 1);
-    const uint32_t idesc3 = make_idesc_bf16(64, RKP, 1, 1);
     bool ok = true;
-    auto mma23 = [&](int j) -> bool {
+    auto mma2 = [&](int j) -> bool {
       const int p = j % NP, sj = j % kBwdStages;
       if (!mbar_wait(&pf_bar[p], (j / NP) & 1, kErrWaitMma, &abort_flag)) return false;
-      if (!mbar_wait(&dze_bar[j & 1], ((j >> 1) & 1) ^ 1, kErrWaitMma, &abort_flag)) return false;
       tc_fence_after();
       if (lane == 0) {
         const uint32_t zb = smem_u32(smem + L::kOffZ + sj * L::kZStride);
-        const uint32_t pb = pb0 + p * W * L::kPTap;
 #pragma unroll
         for (int w = 0; w < W; ++w) {
 #pragma unroll
-          for (int ks = 0; ks < kBT / 16; ++ks) {  // MMA-2: K = timesteps
-            const uint64_t ad = make_smem_desc(pb + w * L::kPTap + ks * 256, 128, L::kPChunk);
+          for (int ks = 0; ks < kBT / 16; ++ks) {  // K = timesteps
             const uint64_t bd = make_smem_desc(zb + ks * 256, 128, L::kZChunk);
-            umma_f16(tmem + L::kColDU + w * RKP, ad, bd, idesc2, (j == 0 && ks == 0) ? 0u : 1u);
+            const uint32_t acc = (j == 0 && ks == 0) ? 0u : 1u;
+            if constexpr (L::kPT) {
+              umma_f16_ts(tmem + L::kColDU + w * RKP, tmem + L::kColPT + w * 32 + ks * 8, bd, idesc2, acc);
+            } else {
+              const uint64_t ad = make_smem_desc(pb0 + p * W * L::kPTap + w * L::kPTap + ks * 256, 128, L::kPChunk);
+              umma_f16(tmem + L::kColDU + w * RKP, ad, bd, idesc2, acc);
+            }
           }
         }
-#pragma unroll
-        for (int w = 0; w < W; ++w) {
-#pragma unroll
-          for (int ks = 0; ks < kBD / 16; ++ks) {  // MMA-3: K = (tap, channel)
-            const uint64_t ad = make_smem_desc(pb + w * L::kPTap + ks * 2 * L::kPChunk, L::kPChunk, 128);
-            const uint64_t bd = make_smem_desc(ub + w * L::kUTap + ks * 2 * L::kUChunk, L::kUChunk, 128);
-            umma_f16(tmem + L::kColDZ + (j & 1) * RKP, ad, bd, idesc3, (w == 0 && ks == 0) ? 0u : 1u);
-          }
-        }
-        umma_commit(&dzf_bar[j & 1]);
-        umma_commit(&pe_bar[p]);
+        if constexpr (L::kPT) umma_commit(&pte_bar);
+        else umma_commit(&pe_bar[p]);
         umma_commit(&empty_bar[sj]);
       }
       __syncwarp();
@@ -591,79 +637,77 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
 #pragma unroll
           for (int w = 0; w < W; ++w) {
 #pragma unroll
-            for (int ks = 0; ks < RKP / 16; ++ks) {  // MMA-1: z rows from 32h + w
-              const uint64_t ad = make_smem_desc(ub + w * L::kUTap + ks * 256, 128, L::kUChunk);
+            for (int ks = 0; ks < RKP / 16; ++ks) {  // z rows from 32h + w
               const uint64_t bd = make_smem_desc(zb + (32 * h + w) * 16 + ks * 2 * L::kZChunk, L::kZChunk, 128);
-              umma_f16(tmem + L::kColA1 + h * 32 * W + w * 32, ad, bd, idesc1, ks > 0 ? 1u : 0u);
+              umma_f16_ts(tmem + L::kColA1 + h * 32 * W + w * 32, tmem + L::kColUA + w * (RKP / 2) + ks * 8, bd,
+                          idesc1, ks > 0 ? 1u : 0u);
             }
           }
           umma_commit(&a1f_bar[h]);
         }
         __syncwarp();
       }
-      if (ok && k >= 1) ok = mma23(k - 1);
+      if (ok && k >= 1) ok = mma2(k - 1);
     }
-    if (ok && n >= 1) ok = mma23(n - 1);
+    if (ok && n >= 1) ok = mma2(n - 1);
     if (lane == 0) umma_commit(&du_bar);
     __syncwarp();
+  } else if (warp == 2) {
+    // ------------------------------------------------------------ MMA-3 issuer
+    const uint32_t ub = smem_u32(smem + L::kOffU), pb0 = smem_u32(smem + L::kOffP);
+    const uint32_t idesc3 = make_idesc_bf16(64, RKP, 1, 1);
+    for (int j = 0; j < n; ++j) {
+      const int p = j % NP;
+      if (!mbar_wait(&pf_bar[p], (j / NP) & 1, kErrWaitMma, &abort_flag)) break;
+      if (!mbar_wait(&dze_bar[j & 1], ((j >> 1) & 1) ^ 1, kErrWaitMma, &abort_flag)) break;
+      tc_fence_after();
+      if (lane == 0) {
+        const uint32_t pb = pb0 + p * W * L::kPTap;
+#pragma unroll
+        for (int w = 0; w < W; ++w) {
+#pragma unroll
+          for (int ks = 0; ks < kBD / 16; ++ks) {  // K = (tap, channel)
+            const uint64_t ad = make_smem_desc(pb + w * L::kPTap + ks * 2 * L::kPChunk, L::kPChunk, 128);
+            const uint64_t bd = make_smem_desc(ub + w * L::kUTap + ks * 2 * L::kUChunk, L::kUChunk, 128);
+            umma_f16(tmem + L::kColDZ + (j & 1) * RKP, ad, bd, idesc3, (w == 0 && ks == 0) ? 0u : 1u);
+          }
+        }
+        umma_commit(&dzf_bar[j & 1]);
+        umma_commit(&pe_bar[p]);
+      }
+      __syncwarp();
+    }
   } else {
     // ------------------------------------------------------------ epilogue
-    const int e = warp - 2;
-    const int q = warp & 3;
-    const int pp = e >> 2;
+    const int e = warp - kBwdCtl;
+    const int q = warp & 3;   // TMEM lane quarter this warp may access
+    const int pp = e >> 2;    // 8-step piece of each 32-step half
     const int ch = q * 32 + lane;
-    const int et = e * 32 + lane;
     const bool dok = d0 + ch < D;
     const uint32_t lane_base = (uint32_t)(q * 32) << 16;
     bool dead = false;
+    constexpr int PC = kBwdPiece;
 
+    // dz partial of tile j (M = 64 layout: lanes 0..15 of quarter q hold steps 16q..16q+15;
+    // the four warps of a quarter take RKP/4 columns each) -> workspace
     auto dz_readout = [&](int j) {
-      const int tile = j0 + j, b = tile / sp.tiles_row, t0 = (tile % sp.tiles_row) * kBT;
+      const int tile = j0 + j;
       if (!dead) dead = !mbar_wait(&dzf_bar[j & 1], (j >> 1) & 1, kErrWaitEpilogue, &abort_flag);
       tc_fence_after();
-      constexpr int NH = RKP / 2;
-      float v[NH];
-      const int c0 = pp * NH;
+      constexpr int NC = RKP / 4;
+      float v[NC];
+      const int c0 = pp * NC;
       if (!dead) {
-        tmem_ld_n<NH>(tmem + lane_base + L::kColDZ + (j & 1) * RKP + c0, v);
+        tmem_ld_n<NC>(tmem + lane_base + L::kColDZ + (j & 1) * RKP + c0, v);
         tmem_ld_wait();
       }
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&dze_bar[j & 1]);
-      const int tok = 16 * q + lane;  // M = 64 layout: lanes 0..15 of each quarter
       if (!dead && lane < 16) {
-        float* dst = dzp + (((size_t)dblk * sp.n_tiles + tile) * kBT + tok) * RKP + c0;
+        float* dst = dzp + (((size_t)dblk * sp.n_tiles + tile) * kBT + 16 * q + lane) * RKP + c0;
 #pragma unroll
-        for (int i = 0; i < NH; i += 4) *reinterpret_cast<float4*>(dst + i) = make_float4(v[i], v[i + 1], v[i + 2], v[i + 3]);
-      }
-      __threadfence();
-      named_bar_sync(2, 32 * kEpiWarps);
-      if (et == 0) last_flag = (!dead && atomicAdd(&cnt[tile], 1) == sp.n_dblk - 1) ? 1 : 0;
-      named_bar_sync(2, 32 * kEpiWarps);
-      if (last_flag && lane < 16) {
-        __threadfence();
-        float acc[NH];
-#pragma unroll
-        for (int i = 0; i < NH; ++i) acc[i] = 0.f;
-        for (int k2 = 0; k2 < sp.n_dblk; ++k2) {
-          const float* src = dzp + (((size_t)k2 * sp.n_tiles + tile) * kBT + tok) * RKP + c0;
-#pragma unroll
-          for (int i = 0; i < NH; i += 4) {
-            const float4 f = __ldcg(reinterpret_cast<const float4*>(src + i));
-            acc[i] += f.x;
-            acc[i + 1] += f.y;
-            acc[i + 2] += f.z;
-            acc[i + 3] += f.w;
-          }
-        }
-        const int t = t0 + tok;
-        if (t < T) {
-          __nv_bfloat16* dst = dz + ((size_t)b * T + t) * R;
-#pragma unroll
-          for (int i = 0; i < NH; ++i)
-            if (c0 + i < R) dst[c0 + i] = __float2bfloat16_rn(acc[i]);
-        }
+        for (int i = 0; i < NC; i += 4) *reinterpret_cast<float4*>(dst + i) = make_float4(v[i], v[i + 1], v[i + 2], v[i + 3]);
       }
     };
 
@@ -680,38 +724,38 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
         if (!dead) dead = !mbar_wait(&a1f_bar[h], k & 1, kErrWaitEpilogue, &abort_flag);
         tc_fence_after();
         if (!dead) {
-          const int tb = 32 * h + 16 * pp;
-          float acc[W][16];
+          const int tb = 32 * h + PC * pp;
+          float acc[W][PC];
 #pragma unroll
-          for (int w = 0; w < W; ++w) tmem_ld16(tmem + lane_base + L::kColA1 + h * 32 * W + w * 32 + 16 * pp, acc[w]);
-          float dyr[16 + W - 1], xr[16 + W - 1];
+          for (int w = 0; w < W; ++w) tmem_ld_n<PC>(tmem + lane_base + L::kColA1 + h * 32 * W + w * 32 + PC * pp, acc[w]);
+          float dyr[PC + W - 1], xr[PC + W - 1];
 #pragma unroll
-          for (int j = 0; j < 16 + W - 1; ++j) {
+          for (int j = 0; j < PC + W - 1; ++j) {
             dyr[j] = __bfloat162float(dys[(tb + j) * kBD + ch]);  // dy at step tb + j
             xr[j] = __bfloat162float(xs[(tb + j) * kBD + ch]);    // x at step tb - (W-1) + j
           }
           tmem_ld_wait();
           __nv_bfloat16* dxc = dx + ((size_t)b * T + t0 + tb) * D + d0 + ch;
 #pragma unroll
-          for (int j = 0; j < 16; ++j) {
+          for (int j = 0; j < PC; ++j) {
             float v = 0.f;
 #pragma unroll
             for (int w = 0; w < W; ++w) v = fmaf(acc[w][j], dyr[j + w], v);
             if (residual) v += dyr[j];
             if (dok && t0 + tb + j < T) dxc[(size_t)j * D] = __float2bfloat16_rn(v);
           }
+          // P^T in TMEM is single-buffered: wait for the MMA-2 of the previous tile
+          if (L::kPT && h == 0) dead = !mbar_wait(&pte_bar, (k & 1) ^ 1, kErrWaitEpilogue, &abort_flag);
+          if (!dead) {
 #pragma unroll
-          for (int w = 0; w < W; ++w) {
+            for (int w = 0; w < W; ++w) {
+              uint32_t pk[PC / 2];
 #pragma unroll
-            for (int hh = 0; hh < 2; ++hh) {
-              __align__(16) __nv_bfloat162 pk[4];
-#pragma unroll
-              for (int i = 0; i < 4; ++i) {
-                const int j = 8 * hh + 2 * i;
-                pk[i] = __floats2bfloat162_rn(dyr[j] * xr[j + W - 1 - w], dyr[j + 1] * xr[j + W - w]);
-              }
-              *reinterpret_cast<uint4*>(pbuf + w * L::kPTap + kmajor_off(ch, tb + 8 * hh, L::kPChunk, 128)) =
-                  *reinterpret_cast<uint4*>(pk);
+              for (int i = 0; i < PC / 2; ++i)
+                pk[i] = pack_bf16x2(dyr[2 * i] * xr[2 * i + W - 1 - w], dyr[2 * i + 1] * xr[2 * i + W - w]);
+              *reinterpret_cast<uint4*>(pbuf + w * L::kPTap + kmajor_off(ch, tb, L::kPChunk, 128)) =
+                  make_uint4(pk[0], pk[1], pk[2], pk[3]);
+              if constexpr (L::kPT) tmem_st4(tmem + lane_base + L::kColPT + w * 32 + tb / 2, pk);
             }
           }
         }
@@ -720,6 +764,8 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
         if (lane == 0) mbar_arrive(&a1e_bar[h]);
       }
       fence_proxy_async_smem();
+      if constexpr (L::kPT) tmem_st_wait();
+      tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&pf_bar[p]);
       if (k >= 1) dz_readout(k - 1);
@@ -746,6 +792,59 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
     }
   }
 
+  // ---------------------------------------------------------------- dz reduction
+  // Publish this CTA's dz partials (CTA barrier, then one cumulative gpu-scope
+  // fence), wait for the other channel-block CTAs of the group, then sum this
+  // CTA's 1/n_dblk slice of the group's (step, rank) pairs in channel-block order.
+  tc_fence_before();
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    __threadfence();
+    atomicAdd(&grp_done[g], 1);
+    bool ok = !abort_flag;
+    if (ok) {
+      const volatile int* gd = grp_done + g;
+      const uint64_t tstart = globaltimer_ns();
+      while (*gd < sp.n_dblk) {
+        if (globaltimer_ns() - tstart > kWaitLimitNs) {
+          atomicCAS(&g_device_error, 0u, (unsigned)kErrWaitTail);
+          ok = false;
+          break;
+        }
+      }
+    }
+    __threadfence();
+    grp_ok = ok ? 1 : 0;
+  }
+  __syncthreads();
+  if (grp_ok) {
+    const int64_t nsteps = (int64_t)n * kBT;
+    const int64_t lo = nsteps * dblk / sp.n_dblk, hi = nsteps * (dblk + 1) / sp.n_dblk;
+    constexpr int RQ = RKP / 4;  // float4 groups per step
+    for (int64_t e2 = lo * RQ + threadIdx.x; e2 < hi * RQ; e2 += blockDim.x) {
+      const int64_t st = e2 / RQ;
+      const int rq = (int)(e2 % RQ);
+      const int tile = j0 + (int)(st / kBT), tok = (int)(st % kBT);
+      const int b = tile / sp.tiles_row, t = (tile % sp.tiles_row) * kBT + tok;
+      float4 a4 = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll 4
+      for (int k2 = 0; k2 < sp.n_dblk; ++k2) {
+        const float4 f =
+            __ldcg(reinterpret_cast<const float4*>(dzp + (((size_t)k2 * sp.n_tiles + tile) * kBT + tok) * RKP) + rq);
+        a4.x += f.x;
+        a4.y += f.y;
+        a4.z += f.z;
+        a4.w += f.w;
+      }
+      if (t < T) {
+        __nv_bfloat16* dst = dz + ((size_t)b * T + t) * R;
+        const float av[4] = {a4.x, a4.y, a4.z, a4.w};
+#pragma unroll
+        for (int i = 0; i < 4; ++i)
+          if (4 * rq + i < R) dst[4 * rq + i] = __float2bfloat16_rn(av[i]);
+      }
+    }
+  }
   tc_fence_before();
   __syncthreads();
   if (warp == 1) tmem_dealloc(tmem, L::kAlloc);
@@ -766,7 +865,7 @@ BwdWorkspace bwd_workspace(void* base, int64_t B, int64_t T, int64_t D, int Rk, 
   const int rkp = Rk <= 16 ? 16 : 32;
   BwdWorkspace w;
   const size_t dzp = al256((size_t)sp.n_dblk * sp.n_tiles * kBT * rkp * sizeof(float));
-  const size_t cnt = al256((size_t)sp.n_tiles * sizeof(int));
+  const size_t cnt = al256((size_t)sp.n_groups * sizeof(int));
   const size_t dUp = al256((size_t)sp.n_groups * Rk * W * D * sizeof(float));
   const size_t zp = zpack_bytes(B, T, rkp);
   uint8_t* p = (uint8_t*)base;
@@ -793,17 +892,34 @@ int launch_bwd(const void* x, const void* z, const void* U, const void* sw, cons
   if ((s = make_btd_map(&xmap, x, B, T, D, kBD, kBT + W - 1))) return s;
   if ((s = make_zpack_map(&zmap, ws.zp, B, T, RKP, kZRows))) return s;
   if ((s = z_pack_launch(z, ws.zp, B, T, R, RKP, sw != nullptr, st))) return s;
-  cudaError_t e = cudaMemsetAsync(ws.cnt, 0, (size_t)sp.n_tiles * sizeof(int), st);
-  if (e != cudaSuccess) return cuda_status(e, "cudaMemsetAsync(tile counters)");
+  cudaError_t e = cudaMemsetAsync(ws.cnt, 0, (size_t)sp.n_groups * sizeof(int), st);
+  if (e != cudaSuccess) return cuda_status(e, "cudaMemsetAsync(group counters)");
   const int smem = (int)L::kTotal;
   e = cudaFuncSetAttribute(lr_bwd_tc_kernel<W, RKP, NP>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
   if (e != cudaSuccess) {
     cudaGetLastError();
     return cuda_status(e, "cudaFuncSetAttribute(lr_bwd_tc)");
   }
-  lr_bwd_tc_kernel<W, RKP, NP><<<sp.n_dblk * sp.n_groups, kBwdThreads, smem, st>>>(
-      dymap, xmap, zmap, (const __nv_bfloat16*)U, (const __nv_bfloat16*)sw, (__nv_bfloat16*)dx, (__nv_bfloat16*)dz,
-      ws.dzp, ws.cnt, ws.dUp, sp, (int)T, (int)D, R, Rk, residual);
+  // Cooperative launch: the CTAs of a token group wait for one another before
+  // the dz reduction, so the whole grid must be co-resident (grid <= SM count,
+  // one CTA per SM; lr_tc_bwd_supported checks the first bound).
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3((unsigned)(sp.n_dblk * sp.n_groups));
+  cfg.blockDim = dim3(kBwdThreads);
+  cfg.dynamicSmemBytes = (size_t)smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeCooperative;
+  attr[0].val.cooperative = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  e = cudaLaunchKernelEx(&cfg, lr_bwd_tc_kernel<W, RKP, NP>, dymap, xmap, zmap, (const __nv_bfloat16*)U,
+                         (const __nv_bfloat16*)sw, (__nv_bfloat16*)dx, (__nv_bfloat16*)dz, ws.dzp, ws.cnt, ws.dUp, sp,
+                         (int)T, (int)D, R, Rk, residual);
+  if (e != cudaSuccess) {
+    cudaGetLastError();
+    return cuda_status(e, "cudaLaunchKernelEx(lr_bwd_tc_kernel)");
+  }
   DYNCONV_CHECK_LAUNCH("lr_bwd_tc_kernel");
   const int64_t nacc = (int64_t)Rk * W * D;
   if ((s = reduce_partials_launch(ws.dUp, sp.n_groups, nacc, dU_f32, nullptr, DYNCONV_DTYPE_BF16, st))) return s;
@@ -835,6 +951,7 @@ bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 
 // CUDA-core kernels of lowrank_simple.cu.
 bool lr_tc_bwd_supported(int64_t D, int Rk, int W, int dtype, const void* const* ptrs, int nptrs) {
   if (dtype != DYNCONV_DTYPE_BF16 || W < 1 || W > 4 || Rk < 1 || Rk > 32 || D % 8 != 0) return false;
+  if ((D + kBD - 1) / kBD > sm_count()) return false;  // the cooperative grid must fit on the GPU
   for (int i = 0; i < nptrs; ++i)
     if (ptrs[i] && !aligned16(ptrs[i])) return false;
   return encode_fn() != nullptr || nptrs == 0;
