@@ -35,6 +35,7 @@ _SIGNATURES = {
     "dynconv_hw_bwd": (_c_int, [_c_vp] * 8 + [_c_vp, _c_size] + [_c_i64] * 5 + [_c_int, _c_int, _c_vp]),
     "dynconv_lr_fwd_workspace_bytes": (_c_size, [_c_i64] * 5 + [_c_int, _c_int]),
     "dynconv_lr_fwd": (_c_int, [_c_vp] * 5 + [_c_vp, _c_size] + [_c_i64] * 5 + [_c_int, _c_int, _c_vp]),
+    "dynconv_lr_fwd_noalloc": (_c_int, [_c_vp] * 5 + [_c_i64] * 5 + [_c_int, _c_int, _c_vp]),
     "dynconv_lr_bwd_workspace_bytes": (_c_size, [_c_i64] * 5 + [_c_int, _c_int]),
     "dynconv_lr_bwd": (_c_int, [_c_vp] * 10 + [_c_vp, _c_size] + [_c_i64] * 5 + [_c_int, _c_int, _c_vp]),
     "dynconv_cast_f32": (_c_int, [_c_vp, _c_vp, _c_i64, _c_int, _c_vp]),

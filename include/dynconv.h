@@ -108,6 +108,30 @@ int dynconv_lr_fwd(const void* x, const void* z, const void* U, const void* stat
                    int64_t B, int64_t T, int64_t D, int64_t R, int64_t W,
                    int dtype, int residual, void* stream);
 
+/* Fixed size of the scratch array that dynconv_lr_fwd_noalloc uses (8 MiB per
+ * device): enough for B*T <= 262144 tokens at R_kernel <= 16, 131072 at <= 32. */
+#define DYNCONV_LR_FWD_NOALLOC_SCRATCH_BYTES ((size_t)8 << 20)
+
+/* dynconv_lr_fwd without a caller workspace: no counterpart in the reference.
+ * For callers that cannot allocate device memory at the call -- a host-language
+ * binding (cgo, JNI, plain C) with no access to PyTorch's caching allocator that
+ * must not call cudaMalloc on its hot path (cudaMalloc/cudaFree synchronise the
+ * device), or a server that reserves all memory at start-up.  Allocates nothing:
+ * the scratch is a static device array of DYNCONV_LR_FWD_NOALLOC_SCRATCH_BYTES
+ * bytes inside the library, one per device; nothing in it has to start at zero.
+ * Same arguments and results as dynconv_lr_fwd otherwise.
+ *   - The first call on each device (with that device current) does a one-time
+ *     set-up: it looks up the scratch address, which also loads the library's
+ *     module on that device.  Make that first call before any stream capture.
+ *   - Sizes whose workspace (dynconv_lr_fwd_workspace_bytes) exceeds the scratch
+ *     are rejected with DYNCONV_ERR_WORKSPACE; use dynconv_lr_fwd for those.
+ *   - All calls on one device share the one scratch array: two calls that can
+ *     overlap (different streams, or host threads without ordering between them)
+ *     race on it.  Issue them on one stream, or order them. */
+int dynconv_lr_fwd_noalloc(const void* x, const void* z, const void* U, const void* static_w, void* y,
+                           int64_t B, int64_t T, int64_t D, int64_t R, int64_t W,
+                           int dtype, int residual, void* stream);
+
 /* Workspace for dynconv_lr_bwd (bytes). */
 size_t dynconv_lr_bwd_workspace_bytes(int64_t B, int64_t T, int64_t D, int64_t R, int64_t W,
                                       int dtype, int has_static);
