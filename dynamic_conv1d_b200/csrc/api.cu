@@ -33,6 +33,29 @@ int cuda_status(cudaError_t e, const char* what) {
   return set_error(DYNCONV_ERR_CUDA, "%s: %s", what, cudaGetErrorString(e));
 }
 
+int encode_tensor_map_bf16(CUtensorMap* map, const void* base, int rank, const cuuint64_t* dims,
+                           const cuuint64_t* strides_bytes, const cuuint32_t* box) {
+  using EncodeFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+  static EncodeFn fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<EncodeFn>(p);
+  });
+  if (!fn) return set_error(DYNCONV_ERR_CUDA, "cuTensorMapEncodeTiled unavailable");
+  const cuuint32_t estr[5] = {1, 1, 1, 1, 1};
+  CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, (cuuint32_t)rank, const_cast<void*>(base), dims, strides_bytes,
+                  box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
+                  CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return set_error(DYNCONV_ERR_CUDA, "cuTensorMapEncodeTiled failed (%d)", (int)r);
+  return DYNCONV_OK;
+}
+
 int sm_count() {
   static int cached[64] = {0};
   int dev = 0;
@@ -46,6 +69,13 @@ int sm_count() {
 }
 
 unsigned int lr_tc_error_word();
+unsigned int hw_tma_error_word();
+bool hw_tma_supported(int64_t D, int64_t H, int W, int log2hs, int dtype, const void* const* ptrs, int nptrs);
+int hw_tma_partial_rows(int64_t B, int64_t T, int64_t D, int log2hs);
+int hw_tma_fwd_launch(const void* x, const void* w, const void* sw, void* y, int64_t B, int64_t T, int64_t D, int64_t H,
+                      int W, int log2hs, int residual, cudaStream_t st);
+int hw_tma_bwd_launch(const void* x, const void* w, const void* sw, const void* dy, void* dx, void* dw, float* part,
+                      int64_t B, int64_t T, int64_t D, int64_t H, int W, int log2hs, int residual, cudaStream_t st);
 unsigned int selftest_error_word();
 
 // kernels (other translation units)
@@ -131,7 +161,7 @@ int dynconv_check_device(void* stream) {
   cudaStream_t st = (cudaStream_t)stream;
   cudaError_t e = cudaStreamSynchronize(st);
   if (e != cudaSuccess) return cuda_status(e, "cudaStreamSynchronize");
-  const unsigned int words[2] = {lr_tc_error_word(), selftest_error_word()};
+  const unsigned int words[3] = {lr_tc_error_word(), selftest_error_word(), hw_tma_error_word()};
   for (unsigned int v : words) {
     if (v == 0xFFFFFFFFu) return set_error(DYNCONV_ERR_CUDA, "could not read the device error word");
     if (v != 0) return set_error(DYNCONV_ERR_TIMEOUT, "a device-side bounded wait gave up (site %u)", v);
@@ -149,14 +179,24 @@ int dynconv_hw_fwd(const void* x, const void* weight, const void* static_w, void
   if (l2 < 0) return set_error(DYNCONV_ERR_UNSUPPORTED, "head_size %lld is not a power of two", (long long)(D / H));
   if (B * T == 0) return DYNCONV_OK;
   if (!x || !weight || !y) return set_error(DYNCONV_ERR_ARGUMENT, "hw_fwd: null x/weight/y");
+  const void* ptrs[] = {x, weight, static_w, y};
+  if (hw_tma_supported(D, H, (int)W, l2, dtype, ptrs, 4))
+    return hw_tma_fwd_launch(x, weight, static_w, y, B, T, D, H, (int)W, l2, residual, (cudaStream_t)stream);
   return hw_fwd_launch(x, weight, static_w, y, B, T, D, H, (int)W, l2, dtype, residual, (cudaStream_t)stream);
 }
 
 size_t dynconv_hw_bwd_workspace_bytes(int64_t B, int64_t T, int64_t D, int64_t H, int64_t W, int dtype,
                                       int has_static) {
-  (void)H;
   if (!has_static || B * T == 0) return 0;
-  return align_up((size_t)hw_partial_rows(B, T, D, dtype) * (size_t)W * (size_t)D * sizeof(float));
+  // Sized for either path (pointer alignment can only move a call to the
+  // register-ring kernels, and both fit the larger of the two).
+  int64_t rows = hw_partial_rows(B, T, D, dtype);
+  const int l2 = (H > 0 && D % H == 0) ? log2_exact(D / H) : -1;
+  if (l2 >= 0 && hw_tma_supported(D, H, (int)W, l2, dtype, nullptr, 0)) {
+    const int64_t r2 = hw_tma_partial_rows(B, T, D, l2);
+    if (r2 > rows) rows = r2;
+  }
+  return align_up((size_t)rows * (size_t)W * (size_t)D * sizeof(float));
 }
 
 int dynconv_hw_bwd(const void* x, const void* weight, const void* static_w, const void* dy, void* dx, void* dweight,
@@ -186,6 +226,15 @@ int dynconv_hw_bwd(const void* x, const void* weight, const void* static_w, cons
     if (!workspace || workspace_bytes < need)
       return set_error(DYNCONV_ERR_WORKSPACE, "hw_bwd: workspace %zu < %zu bytes", workspace_bytes, need);
     part = (float*)workspace;
+  }
+  const void* ptrs[] = {x, weight, static_w, dy, dx, dweight};
+  if (hw_tma_supported(D, H, (int)W, l2, dtype, ptrs, 6)) {
+    if ((s = hw_tma_bwd_launch(x, weight, static_w, dy, dx, dweight, part, B, T, D, H, (int)W, l2, residual, st)))
+      return s;
+    if (has_static)
+      return reduce_partials_launch(part, hw_tma_partial_rows(B, T, D, l2), W * D, dstatic_w_f32, dstatic_w, dtype,
+                                    st);
+    return DYNCONV_OK;
   }
   if ((s = hw_bwd_launch(x, weight, static_w, dy, dx, dweight, part, B, T, D, H, (int)W, l2, dtype, residual, st)))
     return s;

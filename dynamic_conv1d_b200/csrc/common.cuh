@@ -28,6 +28,12 @@ int cuda_status(cudaError_t e, const char* what);
 // Number of SMs of the current device (cached per device).
 int sm_count();
 
+// Encodes a tiled, no-swizzle, zero-fill bf16 TMA descriptor (cuTensorMapEncodeTiled,
+// reached through the runtime's driver entry point).  `strides_bytes` has rank-1
+// entries (dimension 0 is dense).  DYNCONV_OK or DYNCONV_ERR_CUDA.
+int encode_tensor_map_bf16(CUtensorMap* map, const void* base, int rank, const cuuint64_t* dims,
+                           const cuuint64_t* strides_bytes, const cuuint32_t* box);
+
 // Counts kernel launches (dynconv_launch_count) -- call once per launch.
 void note_launch(int n = 1);
 
@@ -278,6 +284,12 @@ __device__ __forceinline__ void prefetch_tensormap(const CUtensorMap* map) {
 __device__ __forceinline__ uint64_t policy_evict_first() {
   uint64_t p;
   asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(p));
+  return p;
+}
+
+__device__ __forceinline__ uint64_t policy_evict_normal() {
+  uint64_t p;
+  asm volatile("createpolicy.fractional.L2::evict_normal.b64 %0, 1.0;" : "=l"(p));
   return p;
 }
 
