@@ -211,8 +211,8 @@ constexpr uint64_t kWaitLimitNs = 1500000000ull;  // 1.5 s
 
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, unsigned int site,
                                           volatile int* abort_flag) {
+  if (mbar_try_wait(bar, parity)) return true;  // fast path: phase already complete
   if (*abort_flag) return false;
-  if (mbar_try_wait(bar, parity)) return true;
   const uint64_t t0 = globaltimer_ns();
   for (uint32_t i = 1;; ++i) {
     if (mbar_try_wait(bar, parity)) return true;

@@ -5,22 +5,24 @@
 // (backward kernel) of OliverSieberling/dynamic-conv1d; oracle reference.py:5-20.
 //
 // Both directions stream HBM (no contraction worth a tensor core).  A tile is
-// 256 channels x TR timesteps of one batch row; a CTA keeps one 256-channel block
-// for a contiguous range of tiles (grid = n_dblk x n_groups, about one CTA per SM):
+// 128 channels x TR timesteps of one batch row; a CTA keeps one 128-channel block
+// for a contiguous range of tiles (grid = n_dblk x n_groups, two CTAs per SM):
 //
 //   warp NC (producer, one lane): TMA loads of the tile's x rows (with the W-1
 //       look-behind rows; zero fill for t < 0 and t >= T), and for the backward the
 //       dy and weight rows with their W-1 look-ahead rows, into an S-stage ring
 //       (full / empty mbarriers, every wait bounded);
-//   warps 0..NC-1 (compute): lane l owns the 16-byte vector of channels 8l..8l+7,
+//   warps 0..NC-1 (compute): lane l owns the 8-byte vector of channels 4l..4l+3,
 //       warp c owns rows c*RPT .. c*RPT+RPT-1 of the tile; every operand comes from
-//       shared memory, outputs go straight to HBM as 16-byte stores (a warp writes
-//       512 contiguous bytes per row).
+//       shared memory, outputs go straight to HBM as 8-byte stores (a warp writes
+//       256 contiguous bytes per row).  Four channels per lane keep the per-thread
+//       state (static_w, the dstatic_w sums, the row window) small enough for two
+//       CTAs -- sixteen compute warps -- per SM.
 //
 // Backward reductions:
 //   dweight[b,t,h,w] = sum_{d in head h} dy[b,t,d] x[b,t-w,d]: in-thread over the
-//       thread's channels of the head, then xor shuffles over the hs/8 lanes of a
-//       head (hs >= 8); no shared memory, no atomics;
+//       thread's channels of the head, then xor shuffles over the hs/4 lanes of a
+//       head (hs >= 4); no shared memory, no atomics;
 //   dstatic_w[w,d] = sum_{b,t} dy x_shift: per-thread fp32 sums over all of the
 //       CTA's tiles (its channel block is fixed), a fixed-order sum over the NC
 //       compute warps in shared memory at the end, one fp32 partial row per CTA,
@@ -34,17 +36,19 @@ DYNCONV_DEFINE_ERROR_ACCESSOR(hw_tma_error_word)
 
 namespace {
 
-constexpr int kCB = 256;  // channels per tile (32 lanes x 8)
-constexpr int kNC = 8;    // compute warps
+constexpr int kVec = 4;            // channels per lane (one 8-byte vector)
+constexpr int kCB = 32 * kVec;     // channels per tile
+constexpr int kNC = 8;             // compute warps
 constexpr int kHwThreads = 32 * (kNC + 1);
-constexpr int kSmemCap = 200 * 1024;
+constexpr int kCtasPerSm = 2;
+constexpr int kSmemCap = 100 * 1024;  // per CTA (two per SM)
 
-// Per-instantiation geometry.  K = min(head_size, 8): a thread's 8 channels span
-// HPT = 8 / K heads.
+// Per-instantiation geometry.  K = min(head_size, kVec): a thread's kVec channels
+// span HPT = kVec / K heads.
 template <int K, int W, bool BWD>
 struct HwGeo {
-  static constexpr int HPT = 8 / K;
-  static constexpr int TR = BWD ? 16 : (K == 8 ? 64 : 16);
+  static constexpr int HPT = kVec / K;
+  static constexpr int TR = BWD ? 16 : (K == kVec ? 64 : 16);
   static constexpr int RPT = TR / kNC;
   static_assert(RPT * kNC == TR, "rows per tile must split over the compute warps");
   static constexpr int ROWS_X = TR + W - 1;           // x rows t0-(W-1) .. t0+TR-1
@@ -104,33 +108,123 @@ __device__ __forceinline__ void st_bf16(__nv_bfloat16* p, const __nv_bfloat16 (&
 
 constexpr int pow2_align(int bytes) { return (bytes % 16 == 0) ? 16 : (bytes % 8 == 0) ? 8 : (bytes % 4 == 0) ? 4 : 2; }
 
-__device__ __forceinline__ void unpack8(const uint4& u, float (&f)[8]) {
+using VecT = uint2;  // kVec bf16
+static_assert(sizeof(VecT) == 2 * kVec, "vector type");
+
+__device__ __forceinline__ void unpackv2(const VecT& u, float2 (&f)[kVec / 2]) {
   const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&u);
 #pragma unroll
-  for (int i = 0; i < 4; ++i) {
-    const float2 t = __bfloat1622float2(h[i]);
-    f[2 * i] = t.x;
-    f[2 * i + 1] = t.y;
-  }
+  for (int i = 0; i < kVec / 2; ++i) f[i] = __bfloat1622float2(h[i]);
 }
 
-__device__ __forceinline__ uint4 pack8(const float (&f)[8]) {
-  uint4 u;
+__device__ __forceinline__ VecT packv2(const float2 (&f)[kVec / 2]) {
+  VecT u;
   __nv_bfloat162* h = reinterpret_cast<__nv_bfloat162*>(&u);
 #pragma unroll
-  for (int i = 0; i < 4; ++i) h[i] = __floats2bfloat162_rn(f[2 * i], f[2 * i + 1]);
+  for (int i = 0; i < kVec / 2; ++i) h[i] = __floats2bfloat162_rn(f[i].x, f[i].y);
   return u;
 }
 
+// Packed fp32 pair arithmetic (sm_100 f32x2 instructions, round to nearest even).
+__device__ __forceinline__ float2 fma2(float2 a, float2 b, float2 c) {
+  float2 d;
+  asm("{\n\t.reg .b64 ra, rb, rc, rd;\n\t"
+      "mov.b64 ra, {%2, %3};\n\tmov.b64 rb, {%4, %5};\n\tmov.b64 rc, {%6, %7};\n\t"
+      "fma.rn.f32x2 rd, ra, rb, rc;\n\tmov.b64 {%0, %1}, rd;\n\t}"
+      : "=f"(d.x), "=f"(d.y)
+      : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y), "f"(c.x), "f"(c.y));
+  return d;
+}
+
+__device__ __forceinline__ float2 add2(float2 a, float2 b) {
+  float2 d;
+  asm("{\n\t.reg .b64 ra, rb, rd;\n\t"
+      "mov.b64 ra, {%2, %3};\n\tmov.b64 rb, {%4, %5};\n\t"
+      "add.rn.f32x2 rd, ra, rb;\n\tmov.b64 {%0, %1}, rd;\n\t}"
+      : "=f"(d.x), "=f"(d.y)
+      : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y));
+  return d;
+}
+
+__device__ __forceinline__ float2 mul2(float2 a, float2 b) {
+  float2 d;
+  asm("{\n\t.reg .b64 ra, rb, rd;\n\t"
+      "mov.b64 ra, {%2, %3};\n\tmov.b64 rb, {%4, %5};\n\t"
+      "mul.rn.f32x2 rd, ra, rb;\n\tmov.b64 {%0, %1}, rd;\n\t}"
+      : "=f"(d.x), "=f"(d.y)
+      : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y));
+  return d;
+}
+
+// dweight of one head and row: v[w] holds this lane's partial over its channels;
+// the 2^lg lanes of the head (consecutive, aligned) sum them and write the W taps
+// to dst (row_ok: this lane's row and channels are inside the tensor).  For W = 4
+// and W = 2 the first levels are a reduce-scatter (each lane keeps half of the
+// taps and sends the other half), so a head of 8 lanes costs 4 shuffles instead
+// of 12; every lane writes the taps it ends up owning.
+template <int W>
+__device__ __forceinline__ void head_reduce_store(float (&v)[W], int lane, int lg, bool row_ok, __nv_bfloat16* dst) {
+  constexpr unsigned kAll = 0xffffffffu;
+  if constexpr (W == 4) {
+    if (lg == 0) {
+      if (row_ok) {
+        __align__(8) __nv_bfloat16 o[4];
+#pragma unroll
+        for (int w = 0; w < 4; ++w) o[w] = __float2bfloat16_rn(v[w]);
+        *reinterpret_cast<uint2*>(dst) = *reinterpret_cast<const uint2*>(o);
+      }
+      return;
+    }
+    // level 1 (lanes l, l^1): the odd lane keeps taps 2,3, the even lane taps 0,1
+    const bool up1 = lane & 1;
+    float k0 = up1 ? v[2] : v[0], k1 = up1 ? v[3] : v[1];
+    const float s0 = up1 ? v[0] : v[2], s1 = up1 ? v[1] : v[3];
+    k0 += __shfl_xor_sync(kAll, s0, 1);
+    k1 += __shfl_xor_sync(kAll, s1, 1);
+    if (lg == 1) {
+      if (row_ok) {
+        __nv_bfloat162 o = __floats2bfloat162_rn(k0, k1);
+        *reinterpret_cast<__nv_bfloat162*>(dst + (up1 ? 2 : 0)) = o;
+      }
+      return;
+    }
+    // level 2 (lanes l, l^2): keep one tap
+    const bool up2 = lane & 2;
+    float k = up2 ? k1 : k0;
+    k += __shfl_xor_sync(kAll, up2 ? k0 : k1, 2);
+    for (int o = 4; o < (1 << lg); o <<= 1) k += __shfl_xor_sync(kAll, k, o);
+    if (row_ok && (lane & ((1 << lg) - 1)) < 4) dst[(up1 ? 2 : 0) + (up2 ? 1 : 0)] = __float2bfloat16_rn(k);
+  } else if constexpr (W == 2) {
+    if (lg == 0) {
+      if (row_ok) *reinterpret_cast<__nv_bfloat162*>(dst) = __floats2bfloat162_rn(v[0], v[1]);
+      return;
+    }
+    const bool up1 = lane & 1;
+    float k = up1 ? v[1] : v[0];
+    k += __shfl_xor_sync(kAll, up1 ? v[0] : v[1], 1);
+    for (int o = 2; o < (1 << lg); o <<= 1) k += __shfl_xor_sync(kAll, k, o);
+    if (row_ok && (lane & ((1 << lg) - 1)) < 2) dst[up1 ? 1 : 0] = __float2bfloat16_rn(k);
+  } else {
+    for (int o = 1; o < (1 << lg); o <<= 1)
+#pragma unroll
+      for (int w = 0; w < W; ++w) v[w] += __shfl_xor_sync(kAll, v[w], o);
+    if (row_ok && (lane & ((1 << lg) - 1)) == 0) {
+#pragma unroll
+      for (int w = 0; w < W; ++w) dst[w] = __float2bfloat16_rn(v[w]);
+    }
+  }
+}
+
 // Weights of the thread's heads for one row: wt[j][w] for the head of channel
-// group j (j < HPT; HPT = 1 when the 8 channels share one head).
+// group j (j < HPT; HPT = 1 when the lane's channels share one head).
 template <int K, int W>
-__device__ __forceinline__ void load_row_weights(const __nv_bfloat16* wrow, int lane, int log2hs, float (&wt)[8 / K][W]) {
-  constexpr int HPT = 8 / K;
+__device__ __forceinline__ void load_row_weights(const __nv_bfloat16* wrow, int lane, int log2hs,
+                                                 float (&wt)[kVec / K][W]) {
+  constexpr int HPT = kVec / K;
   constexpr int N = HPT * W;
   __align__(16) __nv_bfloat16 v[N];
-  if constexpr (K == 8) {
-    const int hl = (8 * lane) >> log2hs;  // local head of the block
+  if constexpr (K == kVec) {
+    const int hl = (kVec * lane) >> log2hs;  // local head of the block
     ld_bf16<N, pow2_align(2 * W)>(wrow + hl * W, v);
   } else {
     ld_bf16<N, pow2_align(2 * N)>(wrow + lane * N, v);
@@ -142,7 +236,7 @@ __device__ __forceinline__ void load_row_weights(const __nv_bfloat16* wrow, int 
 }
 
 template <int K, int W, bool BWD>
-__global__ void __launch_bounds__(kHwThreads, 1)
+__global__ void __launch_bounds__(kHwThreads, kCtasPerSm)
     hw_tma_kernel(const __grid_constant__ CUtensorMap xmap, const __grid_constant__ CUtensorMap dymap,
                   const __grid_constant__ CUtensorMap wmap, const __nv_bfloat16* __restrict__ sw,
                   __nv_bfloat16* __restrict__ out, __nv_bfloat16* __restrict__ dw, float* __restrict__ part,
@@ -181,10 +275,14 @@ __global__ void __launch_bounds__(kHwThreads, 1)
       if constexpr (BWD) prefetch_tensormap(&dymap);
       const uint64_t pol = policy_evict_normal();
       const uint32_t bytes = G::X_BYTES + G::DY_BYTES + G::ROWS_A * wb * 2;
-      for (int k = 0; k < n; ++k) {
+      int b = j0 / sp.tiles_row, t0 = (j0 % sp.tiles_row) * TR;
+      for (int k = 0; k < n; ++k, t0 += TR) {
+        if (t0 >= T) {
+          t0 = 0;
+          ++b;
+        }
         const int s = k % S;
         if (!mbar_wait(&empty_bar[s], ((k / S) & 1) ^ 1, kErrWaitProducer, &abort_flag)) break;
-        const int tile = j0 + k, b = tile / sp.tiles_row, t0 = (tile % sp.tiles_row) * TR;
         uint8_t* st = smem + s * G::STAGE;
         mbar_arrive_expect_tx(&full_bar[s], bytes);
         tma_load_3d(st, &xmap, &full_bar[s], d0, t0 - (W - 1), b, pol);
@@ -198,25 +296,30 @@ __global__ void __launch_bounds__(kHwThreads, 1)
   }
 
   // -------------------------------------------------------------- compute
-  const int dch = d0 + 8 * lane;
+  // Channel pairs (c = 2p, 2p+1) are computed with packed fp32 instructions
+  // (fma/add/mul .rn.f32x2): each lane of a pair rounds exactly like the scalar op.
+  constexpr int P = kVec / 2;
+  const int dch = d0 + kVec * lane;
   const bool dok = dch < D;
   const int r0 = warp * RPT;
-  float s_w[W][8];
+  float2 s2[W][P];
 #pragma unroll
   for (int w = 0; w < W; ++w) {
     if (sw != nullptr && dok) {
-      unpack8(*reinterpret_cast<const uint4*>(sw + (size_t)w * D + dch), s_w[w]);
+      unpackv2(*reinterpret_cast<const VecT*>(sw + (size_t)w * D + dch), s2[w]);
     } else {
 #pragma unroll
-      for (int c = 0; c < 8; ++c) s_w[w][c] = 0.f;
+      for (int q = 0; q < P; ++q) s2[w][q] = make_float2(0.f, 0.f);
     }
   }
-  float acc_sw[BWD ? W : 1][8];
+  float2 acc_sw[BWD ? W : 1][P];
 #pragma unroll
   for (int w = 0; w < (BWD ? W : 1); ++w)
 #pragma unroll
-    for (int c = 0; c < 8; ++c) acc_sw[w][c] = 0.f;
+    for (int q = 0; q < P; ++q) acc_sw[w][q] = make_float2(0.f, 0.f);
 
+  // (b, t0) of the current tile, advanced incrementally
+  int b = j0 / sp.tiles_row, t0 = (j0 % sp.tiles_row) * TR;
   bool dead = false;
   for (int k = 0; k < n; ++k) {
     const int s = k % S;
@@ -224,124 +327,113 @@ __global__ void __launch_bounds__(kHwThreads, 1)
       dead = true;
       break;
     }
-    const int tile = j0 + k, b = tile / sp.tiles_row, t0 = (tile % sp.tiles_row) * TR;
     const uint8_t* st = smem + s * G::STAGE;
-    const __nv_bfloat16* xs = reinterpret_cast<const __nv_bfloat16*>(st) + 8 * lane;
+    const __nv_bfloat16* xs = reinterpret_cast<const __nv_bfloat16*>(st) + kVec * lane;
     const __nv_bfloat16* ws = reinterpret_cast<const __nv_bfloat16*>(st + G::X_BYTES + G::DY_BYTES);
 
     if constexpr (!BWD) {
       // x rows r0 .. r0+RPT+W-2 of the tile (step t0 - (W-1) + i)
-      float xr[RPT + W - 1][8];
+      float2 xr[RPT + W - 1][P];
 #pragma unroll
-      for (int i = 0; i < RPT + W - 1; ++i) unpack8(*reinterpret_cast<const uint4*>(xs + (r0 + i) * kCB), xr[i]);
+      for (int i = 0; i < RPT + W - 1; ++i) unpackv2(*reinterpret_cast<const VecT*>(xs + (r0 + i) * kCB), xr[i]);
 #pragma unroll
       for (int rr = 0; rr < RPT; ++rr) {
         const int t = t0 + r0 + rr;
         float wt[HPT][W];
         load_row_weights<K, W>(ws + (r0 + rr) * wb, lane, log2hs, wt);
-        float y[8];
+        float2 y[P];
 #pragma unroll
-        for (int c = 0; c < 8; ++c) {
-          float v = residual ? xr[rr + W - 1][c] : 0.f;
+        for (int q = 0; q < P; ++q) {
+          y[q] = residual ? xr[rr + W - 1][q] : make_float2(0.f, 0.f);
 #pragma unroll
-          for (int w = 0; w < W; ++w) v = fmaf(wt[c / K][w] + s_w[w][c], xr[rr + W - 1 - w][c], v);
-          y[c] = v;
+          for (int w = 0; w < W; ++w) {
+            const float2 coef = add2(make_float2(wt[(2 * q) / K][w], wt[(2 * q + 1) / K][w]), s2[w][q]);
+            y[q] = fma2(coef, xr[rr + W - 1 - w][q], y[q]);
+          }
         }
-        if (dok && t < T) *reinterpret_cast<uint4*>(out + ((size_t)b * T + t) * D + dch) = pack8(y);
+        if (dok && t < T) *reinterpret_cast<VecT*>(out + ((size_t)b * T + t) * D + dch) = packv2(y);
       }
     } else {
-      const __nv_bfloat16* dys = reinterpret_cast<const __nv_bfloat16*>(st + G::X_BYTES) + 8 * lane;
-      // dy rows r0 .. r0+RPT+W-2 (step t0 + i); x rows r0 .. r0+RPT+W-2 (step t0 - (W-1) + i),
-      // kept packed (bf16) and unpacked where used
-      uint4 dyp[RPT + W - 1], xp[RPT + W - 1];
+      const __nv_bfloat16* dys = reinterpret_cast<const __nv_bfloat16*>(st + G::X_BYTES) + kVec * lane;
+      // dy rows r0 .. r0+RPT+W-2 (step t0 + i); x rows r0 .. r0+RPT+W-2 (step t0 - (W-1) + i)
+      float2 dyf[RPT + W - 1][P], xf[RPT + W - 1][P];
 #pragma unroll
       for (int i = 0; i < RPT + W - 1; ++i) {
-        dyp[i] = *reinterpret_cast<const uint4*>(dys + (r0 + i) * kCB);
-        xp[i] = *reinterpret_cast<const uint4*>(xs + (r0 + i) * kCB);
+        unpackv2(*reinterpret_cast<const VecT*>(dys + (r0 + i) * kCB), dyf[i]);
+        unpackv2(*reinterpret_cast<const VecT*>(xs + (r0 + i) * kCB), xf[i]);
       }
       // dx[t] = sum_w (weight[t+w, h, w] + static_w[w]) * dy[t+w]  (+ dy[t]).  Weight row
       // j (step t0 + r0 + j) is read once and feeds dx rows j - w.
-      float dxv[RPT][8];
+      float2 dxv[RPT][P];
 #pragma unroll
-      for (int rr = 0; rr < RPT; ++rr) {
-        if (residual) unpack8(dyp[rr], dxv[rr]);
-        else {
+      for (int rr = 0; rr < RPT; ++rr)
 #pragma unroll
-          for (int c = 0; c < 8; ++c) dxv[rr][c] = 0.f;
-        }
-      }
+        for (int q = 0; q < P; ++q) dxv[rr][q] = residual ? dyf[rr][q] : make_float2(0.f, 0.f);
 #pragma unroll
       for (int j = 0; j < RPT + W - 1; ++j) {
-        float wt[HPT][W], dyf[8];
+        float wt[HPT][W];
         load_row_weights<K, W>(ws + (r0 + j) * wb, lane, log2hs, wt);
-        unpack8(dyp[j], dyf);
 #pragma unroll
         for (int w = 0; w < W; ++w) {
           const int rr = j - w;
           if (rr >= 0 && rr < RPT) {
 #pragma unroll
-            for (int c = 0; c < 8; ++c) dxv[rr][c] = fmaf(wt[c / K][w] + s_w[w][c], dyf[c], dxv[rr][c]);
+            for (int q = 0; q < P; ++q) {
+              const float2 coef = add2(make_float2(wt[(2 * q) / K][w], wt[(2 * q + 1) / K][w]), s2[w][q]);
+              dxv[rr][q] = fma2(coef, dyf[j][q], dxv[rr][q]);
+            }
           }
         }
       }
 #pragma unroll
       for (int rr = 0; rr < RPT; ++rr) {
         const int t = t0 + r0 + rr;
-        // P_w = dy[t] * x[t-w]: dweight (per head) and dstatic_w (per channel)
-        float pw[W][8], dyf[8];
-        unpack8(dyp[rr], dyf);
+        const bool row_ok = dok && t < T;
+        if (row_ok) *reinterpret_cast<VecT*>(out + ((size_t)b * T + t) * D + dch) = packv2(dxv[rr]);
+        // P_w = dy[t] * x[t-w]: dstatic_w (per channel, fused multiply-add) and
+        // dweight (summed over the head's channels)
 #pragma unroll
-        for (int w = 0; w < W; ++w) {
-          float xf[8];
-          unpack8(xp[rr + W - 1 - w], xf);
+        for (int w = 0; w < W; ++w)
 #pragma unroll
-          for (int c = 0; c < 8; ++c) {
-            pw[w][c] = dyf[c] * xf[c];
-            acc_sw[w][c] += pw[w][c];
-          }
-        }
-        const bool row_ok = t < T;
-        if (dok && row_ok) *reinterpret_cast<uint4*>(out + ((size_t)b * T + t) * D + dch) = pack8(dxv[rr]);
-        if constexpr (K == 8) {
+          for (int q = 0; q < P; ++q) acc_sw[w][q] = fma2(dyf[rr][q], xf[rr + W - 1 - w][q], acc_sw[w][q]);
+        if constexpr (K == kVec) {
+          // one head per lane: sum the lane's channels, then over the hs/4 lanes of the head
           float hsum[W];
 #pragma unroll
           for (int w = 0; w < W; ++w) {
-            float v = 0.f;
+            float2 a = mul2(dyf[rr][0], xf[rr + W - 1 - w][0]);
 #pragma unroll
-            for (int c = 0; c < 8; ++c) v += pw[w][c];
-            hsum[w] = v;
+            for (int q = 1; q < P; ++q) a = fma2(dyf[rr][q], xf[rr + W - 1 - w][q], a);
+            hsum[w] = a.x + a.y;
           }
-          const int gl = 1 << (log2hs - 3);  // lanes per head
-          for (int o = 1; o < gl; o <<= 1)
-#pragma unroll
-            for (int w = 0; w < W; ++w) hsum[w] += __shfl_xor_sync(0xffffffffu, hsum[w], o);
-          if (dok && row_ok && (lane & (gl - 1)) == 0) {
-            __align__(16) __nv_bfloat16 v[W];
-#pragma unroll
-            for (int w = 0; w < W; ++w) v[w] = __float2bfloat16_rn(hsum[w]);
-            const int h = dch >> log2hs;
-            st_bf16<W, pow2_align(2 * W)>(dw + (((size_t)b * T + t) * H + h) * W, v);
-          }
+          head_reduce_store<W>(hsum, lane, log2hs - 2, row_ok,
+                               dw + (((size_t)b * T + t) * H + (dch >> log2hs)) * W);
         } else {
+          // HPT heads per lane, K channels each (K = 1 or 2)
           __align__(16) __nv_bfloat16 v[HPT * W];
 #pragma unroll
-          for (int j = 0; j < HPT; ++j)
+          for (int w = 0; w < W; ++w)
 #pragma unroll
-            for (int w = 0; w < W; ++w) {
-              float a = 0.f;
-#pragma unroll
-              for (int c = 0; c < K; ++c) a += pw[w][j * K + c];
-              v[j * W + w] = __float2bfloat16_rn(a);
+            for (int q = 0; q < P; ++q) {
+              const float2 pr = mul2(dyf[rr][q], xf[rr + W - 1 - w][q]);
+              if constexpr (K == 1) {
+                v[(2 * q) * W + w] = __float2bfloat16_rn(pr.x);
+                v[(2 * q + 1) * W + w] = __float2bfloat16_rn(pr.y);
+              } else {
+                v[q * W + w] = __float2bfloat16_rn(pr.x + pr.y);
+              }
             }
-          if (dok && row_ok) {
-            const int h0 = dch / K;
-            st_bf16<HPT * W, pow2_align(2 * HPT * W)>(dw + (((size_t)b * T + t) * H + h0) * W, v);
-          }
+          if (row_ok) st_bf16<HPT * W, pow2_align(2 * HPT * W)>(dw + (((size_t)b * T + t) * H + dch / K) * W, v);
         }
       }
     }
     __syncwarp();
     if (lane == 0) mbar_arrive(&empty_bar[s]);
+    t0 += TR;
+    if (t0 >= T) {
+      t0 = 0;
+      ++b;
+    }
   }
 
   if constexpr (BWD) {
@@ -354,7 +446,10 @@ __global__ void __launch_bounds__(kHwThreads, 1)
 #pragma unroll
       for (int w = 0; w < W; ++w)
 #pragma unroll
-        for (int c = 0; c < 8; ++c) red[(warp * W + w) * kCB + 8 * lane + c] = acc_sw[w][c];
+        for (int q = 0; q < P; ++q) {
+          red[(warp * W + w) * kCB + kVec * lane + 2 * q] = acc_sw[w][q].x;
+          red[(warp * W + w) * kCB + kVec * lane + 2 * q + 1] = acc_sw[w][q].y;
+        }
       named_bar_sync(1, kNC * 32);
       for (int i = threadIdx.x; i < W * kCB; i += kNC * 32) {
         const int w = i / kCB, c = i % kCB;
@@ -372,14 +467,14 @@ HwSplit hw_split(int64_t B, int64_t T, int64_t D, int TR) {
   sp.n_dblk = (int)((D + kCB - 1) / kCB);
   sp.tiles_row = (int)((T + TR - 1) / TR);
   sp.n_tiles = (int)(B * sp.tiles_row);
-  int g = sm_count() / sp.n_dblk;
+  int g = kCtasPerSm * sm_count() / sp.n_dblk;
   if (g < 1) g = 1;
   if (g > sp.n_tiles) g = sp.n_tiles;
   sp.n_groups = g;
   return sp;
 }
 
-int hw_tr(int K, bool bwd) { return bwd ? 16 : (K == 8 ? 64 : 16); }
+int hw_tr(int K, bool bwd) { return bwd ? 16 : (K == kVec ? 64 : 16); }
 
 template <int K, int W, bool BWD>
 int launch_hw_tma(const void* x, const void* wgt, const void* sw, const void* dy, void* out, void* dw, float* part,
@@ -387,7 +482,7 @@ int launch_hw_tma(const void* x, const void* wgt, const void* sw, const void* dy
   using G = HwGeo<K, W, BWD>;
   const HwSplit sp = hw_split(B, T, D, G::TR);
   const int hs = 1 << log2hs;
-  const int wb = (kCB / hs) * W;  // weight elements per tile row (hs <= 256)
+  const int wb = (kCB / hs) * W;  // weight elements per tile row (hs <= kCB)
   const int64_t HW = H * W;
   CUtensorMap xmap, dymap, wmap;
   int s;
@@ -410,10 +505,11 @@ int launch_hw_tma(const void* x, const void* wgt, const void* sw, const void* dy
     const cuuint32_t box[3] = {(cuuint32_t)wb, (cuuint32_t)G::ROWS_A, 1};
     if ((s = encode_tensor_map_bf16(&wmap, wgt, 3, dims, strides, box))) return s;
   } else {
-    wchunks = wb / 256;
-    const cuuint64_t dims[4] = {256, (cuuint64_t)(HW / 256), (cuuint64_t)T, (cuuint64_t)B};
-    const cuuint64_t strides[3] = {512, (cuuint64_t)HW * 2, (cuuint64_t)T * HW * 2};
-    const cuuint32_t box[4] = {256, (cuuint32_t)wchunks, (cuuint32_t)G::ROWS_A, 1};
+    // rows wider than one 256-element box: 128-element chunks as a 4-D box
+    wchunks = wb / 128;
+    const cuuint64_t dims[4] = {128, (cuuint64_t)(HW / 128), (cuuint64_t)T, (cuuint64_t)B};
+    const cuuint64_t strides[3] = {256, (cuuint64_t)HW * 2, (cuuint64_t)T * HW * 2};
+    const cuuint32_t box[4] = {128, (cuuint32_t)wchunks, (cuuint32_t)G::ROWS_A, 1};
     if ((s = encode_tensor_map_bf16(&wmap, wgt, 4, dims, strides, box))) return s;
   }
   auto kern = hw_tma_kernel<K, W, BWD>;
@@ -433,14 +529,13 @@ int launch_hw_tma(const void* x, const void* wgt, const void* sw, const void* dy
 template <bool BWD>
 int hw_tma_dispatch(const void* x, const void* wgt, const void* sw, const void* dy, void* out, void* dw, float* part,
                     int64_t B, int64_t T, int64_t D, int64_t H, int W, int log2hs, int residual, cudaStream_t st) {
-  const int K = log2hs >= 3 ? 8 : (1 << log2hs);
+  const int K = log2hs >= 2 ? 4 : (1 << log2hs);
 #define DYNCONV_HWT(KK, WW)                                                                                       \
   if (K == KK && W == WW)                                                                                         \
     return launch_hw_tma<KK, WW, BWD>(x, wgt, sw, dy, out, dw, part, B, T, D, H, log2hs, residual, st);
   DYNCONV_HWT(1, 1) DYNCONV_HWT(1, 2) DYNCONV_HWT(1, 3) DYNCONV_HWT(1, 4)
   DYNCONV_HWT(2, 1) DYNCONV_HWT(2, 2) DYNCONV_HWT(2, 3) DYNCONV_HWT(2, 4)
   DYNCONV_HWT(4, 1) DYNCONV_HWT(4, 2) DYNCONV_HWT(4, 3) DYNCONV_HWT(4, 4)
-  DYNCONV_HWT(8, 1) DYNCONV_HWT(8, 2) DYNCONV_HWT(8, 3) DYNCONV_HWT(8, 4)
 #undef DYNCONV_HWT
   return set_error(DYNCONV_ERR_UNSUPPORTED, "headwise TMA path: head_size %d, W %d", 1 << log2hs, W);
 }
@@ -449,23 +544,23 @@ bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) ==
 
 }  // namespace
 
-// Envelope of the TMA path: bf16, W <= 4, D % 8 == 0, head_size <= 256, a tile
-// row of weights ((256 / head_size) * W elements) a multiple of 16 bytes (and of
-// 256 elements, with H*W too, when it exceeds one 256-element TMA box), 16-byte
+// Envelope of the TMA path: bf16, W <= 4, D % 8 == 0, head_size <= 128, a tile
+// row of weights ((128 / head_size) * W elements) a multiple of 16 bytes (and of
+// 128 elements, with H*W too, when it exceeds one 256-element TMA box), 16-byte
 // aligned tensors.  Everything else runs the register-ring kernels of headwise.cu.
 bool hw_tma_supported(int64_t D, int64_t H, int W, int log2hs, int dtype, const void* const* ptrs, int nptrs) {
-  if (dtype != DYNCONV_DTYPE_BF16 || W < 1 || W > 4 || D % 8 != 0 || log2hs > 8) return false;
+  if (dtype != DYNCONV_DTYPE_BF16 || W < 1 || W > 4 || D % 8 != 0 || log2hs > 7) return false;
   const int64_t wb = (int64_t)(kCB >> log2hs) * W;
   const int64_t HW = H * W;
   if (wb % 8 != 0 || HW % 8 != 0) return false;
-  if (wb > 256 && (wb % 256 != 0 || HW % 256 != 0)) return false;
+  if (wb > 256 && (wb % 128 != 0 || HW % 128 != 0)) return false;
   for (int i = 0; i < nptrs; ++i)
     if (ptrs[i] && !aligned16(ptrs[i])) return false;
   return true;
 }
 
 int hw_tma_partial_rows(int64_t B, int64_t T, int64_t D, int log2hs) {
-  return hw_split(B, T, D, hw_tr(log2hs >= 3 ? 8 : 1, true)).n_groups;
+  return hw_split(B, T, D, hw_tr(log2hs >= 2 ? kVec : 1, true)).n_groups;
 }
 
 int hw_tma_fwd_launch(const void* x, const void* w, const void* sw, void* y, int64_t B, int64_t T, int64_t D, int64_t H,

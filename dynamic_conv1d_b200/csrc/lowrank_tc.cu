@@ -16,14 +16,16 @@
 //        -> TMEM acc_w[ch][t] = sum_r U[r,w,ch] z[t,r]      (the dynamic weights;
 //                                                            never written to HBM)
 //   epilogue warps: y[t,ch] = sum_w acc_w[ch][t] * x[t-w,ch] (+ x[t,ch])
-//        -> smem y tile -> TMA store
+//        -> per-warp smem y sub-tile [32 steps][32 ch] -> TMA store issued by the warp
 //
 // Warp roles (320 threads, one CTA per SM, persistent over a contiguous range
 // of work items):  warp 0 producer, warp 1 TMEM owner + MMA issuer (one lane),
 // warps 2..9 epilogue (two warps per TMEM lane quarter, one per 32-step half).
 // Pipelines: S-stage x/z ring (full/empty mbarriers), double-buffered TMEM
-// accumulators (acc_full via tcgen05.commit / acc_empty), double-buffered y tile
-// (TMA store bulk groups).  Every mbarrier wait is bounded (common.cuh).
+// accumulators (acc_full via tcgen05.commit / acc_empty), a double-buffered y
+// sub-tile per epilogue warp (the warp's own TMA store bulk groups), so the
+// epilogue warps never synchronise with one another.  Every mbarrier wait is
+// bounded (common.cuh).
 #include <mutex>
 
 #include "common.cuh"
@@ -157,12 +159,12 @@ struct FwdSmem {
   static constexpr uint32_t kXBytes = (uint32_t)kXRows * kBD * 2;        // TMA box bytes
   static constexpr uint32_t kXStride = (kXBytes + 1023u) / 1024u * 1024u;
   static constexpr uint32_t kZBytes = (uint32_t)kBT * RKP * 2;           // K-major, 64 rows x RKP
-  static constexpr uint32_t kYBytes = (uint32_t)kBT * kBD * 2;
+  static constexpr uint32_t kYWarpBytes = 32 * 32 * 2;  // one epilogue warp's y sub-tile [32 steps][32 ch]
   static constexpr uint32_t kUTap = (uint32_t)kBD * RKP * 2;
   static constexpr uint32_t kOffX = 0;
   static constexpr uint32_t kOffZ = kOffX + kS * kXStride;
-  static constexpr uint32_t kOffY = kOffZ + kS * kZBytes;
-  static constexpr uint32_t kOffU = kOffY + 2 * kYBytes;
+  static constexpr uint32_t kOffY = kOffZ + kS * kZBytes;  // [kEpiWarps][2 buffers][kYWarpBytes]
+  static constexpr uint32_t kOffU = kOffY + kEpiWarps * 2 * kYWarpBytes;
   static constexpr uint32_t kTotal = kOffU + W * kUTap + 1024;  // + alignment slack
   // K-major operand strides
   static constexpr uint32_t kZLbo = kBT * 16;          // next 8-rank chunk of z
@@ -297,19 +299,18 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
     const int q = warp & 3;            // TMEM lane quarter this warp may access
     const int half = e >> 2;           // which 32-step half of the tile
     const int ch = q * 32 + lane;      // channel within the block (= TMEM lane)
-    const int et = e * 32 + lane;      // 0..255
     const uint64_t pol_y = policy_evict_first();
-    bool dead = false;  // a bounded wait gave up: keep joining the named barriers, skip the work
+    bool dead = false;  // a bounded wait gave up: skip the work, keep arriving
     for (int k = 0; k < n; ++k) {
       const int s = k % S, a = k & 1;
       const int tile = j0 + k, b = tile / sp.tiles_row, t0 = (tile % sp.tiles_row) * kBT;
-      // y buffer `a` is free once the store issued two items ago has read it
-      if (et == 0 && !dead) bulk_wait_group_read<1>();
-      named_bar_sync(1, 32 * kEpiWarps);
+      // this warp's y buffer (k & 1) is free once its store of item k-2 has read it
+      if (lane == 0 && !dead) bulk_wait_group_read<1>();
+      __syncwarp();
       if (!dead) dead = !mbar_wait(&full_bar[s], (k / S) & 1, kErrWaitEpilogue, &abort_flag);
       if (!dead) dead = !mbar_wait(&accf_bar[a], (k >> 1) & 1, kErrWaitEpilogue, &abort_flag);
       tc_fence_after();
-      __nv_bfloat16* ys = reinterpret_cast<__nv_bfloat16*>(smem + L::kOffY + a * L::kYBytes);
+      __nv_bfloat16* ys = reinterpret_cast<__nv_bfloat16*>(smem + L::kOffY + (e * 2 + a) * L::kYWarpBytes);
       if (!dead) {
         const __nv_bfloat16* xs = reinterpret_cast<const __nv_bfloat16*>(smem + L::kOffX + s * L::kXStride);
         // x window: xr[j] = x at step (tok0 - (W-1) + j); smem row of step t is (t - t0) + (W-1)
@@ -333,26 +334,25 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
 #pragma unroll
             for (int w = 0; w < W; ++w) yv = fmaf(acc[w][j], xr[W - 1 + j - w], yv);
             if (residual) yv += xr[W - 1 + j];
-            ys[(tb + j) * kBD + ch] = __float2bfloat16_rn(yv);
+            ys[(c * 16 + j) * 32 + lane] = __float2bfloat16_rn(yv);
           }
 #pragma unroll
           for (int j = 0; j < W - 1; ++j) xr[j] = xr[16 + j];
         }
       }
       tc_fence_before();
+      fence_proxy_async_smem();
       __syncwarp();
       if (lane == 0) {
         mbar_arrive(&acce_bar[a]);
         mbar_arrive(&empty_bar[s]);
-      }
-      fence_proxy_async_smem();
-      named_bar_sync(1, 32 * kEpiWarps);
-      if (et == 0 && !dead) {
-        tma_store_3d(&ymap, ys, d0, t0, b, pol_y);
-        bulk_commit_group();
+        if (!dead) {
+          tma_store_3d(&ymap, ys, d0 + q * 32, t0 + half * 32, b, pol_y);
+          bulk_commit_group();
+        }
       }
     }
-    if (et == 0) bulk_wait_group<0>();
+    if (lane == 0) bulk_wait_group<0>();
   }
 
   tc_fence_before();
@@ -368,7 +368,7 @@ int launch_fwd(const void* x, const void* z, const void* U, const void* sw, void
   CUtensorMap xmap, ymap, zmap;
   int s;
   if ((s = make_btd_map(&xmap, x, B, T, D, kBD, kBT + W - 1))) return s;
-  if ((s = make_btd_map(&ymap, y, B, T, D, kBD, kBT))) return s;
+  if ((s = make_btd_map(&ymap, y, B, T, D, 32, 32))) return s;  // per-warp [32 steps][32 ch] stores
   if ((s = make_zpack_map(&zmap, ws, B, T, RKP, kBT))) return s;
   if ((s = z_pack_launch(z, ws, B, T, R, RKP, sw != nullptr, st))) return s;
   const TileSplit sp = tile_split(B, T, D);
