@@ -221,7 +221,6 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
   const int j0 = (int)((int64_t)sp.n_tiles * g / sp.n_groups);
   const int n = (int)((int64_t)sp.n_tiles * (g + 1) / sp.n_groups) - j0;
   const int d0 = dblk * kBD;
-  const bool has_static = sw != nullptr;
   constexpr uint32_t kAccCols = W * kBT;
   constexpr uint32_t kTmemCols = (2 * kAccCols <= 256) ? 256 : 512;
 
@@ -242,17 +241,23 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
     prefetch_tensormap(&ymap);
     prefetch_tensormap(&zmap);
   }
-  // U block of this CTA's channels, loaded once by every thread (MMA A operand).
-  load_u_block<W, RKP>(smem + L::kOffU, U, sw, dblk, D, R, threadIdx.x, blockDim.x);
-  fence_proxy_async_smem();
-  if (warp == 1) {
-    tmem_alloc(&tmem_slot, kTmemCols);
-    tmem_relinquish();
+  __syncthreads();  // barriers initialised: the producer starts its loads at once
+  uint32_t tmem = 0;
+  if (warp != 0) {
+    // U block of this CTA's channels (MMA A operand), loaded once by all but the
+    // producer, then the TMEM allocation.
+    constexpr int kNonProducer = kFwdThreads - 32;
+    load_u_block<W, RKP>(smem + L::kOffU, U, sw, dblk, D, R, threadIdx.x - 32, kNonProducer);
+    fence_proxy_async_smem();
+    if (warp == 1) {
+      tmem_alloc(&tmem_slot, kTmemCols);
+      tmem_relinquish();
+    }
+    tc_fence_before();
+    named_bar_sync(2, kNonProducer);
+    tc_fence_after();
+    tmem = tmem_slot;
   }
-  tc_fence_before();
-  __syncthreads();
-  tc_fence_after();
-  const uint32_t tmem = tmem_slot;
 
   if (warp == 0) {
     // ------------------------------------------------------------ producer
@@ -410,7 +415,9 @@ int launch_fwd_w(int W, const void* x, const void* z, const void* U, const void*
 //             does before its dots, lowrank.py:128) -> smem, and transposed -> TMEM
 //   MMA-2  dU_w[ch][r] += sum_t P_w[t,ch] z[t,r]       M=128 ch, N=R_kernel, K=64 t
 //          A = P^T from TMEM (R_kernel <= 16; else from smem), B = z (MN-major view);
-//          accumulated in TMEM over all items of the CTA, one partial block per CTA.
+//          accumulated in TMEM over all items of the CTA, one partial block per CTA;
+//          after a grid-wide count (cooperative launch) every CTA sums a slice of the
+//          partials in group order and writes dU_f32, dU and dstatic_w itself.
 //   MMA-3  dz[t][r]     = sum_{w,ch} P_w[t,ch] U[r,w,ch] M=64 t,  N=R_kernel, K=128*W
 //          A = P (smem, MN-major view), B = U (smem); partial over this CTA's 128
 //          channels, written to the workspace.  After its last tile every CTA of a
@@ -491,7 +498,8 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
                      const __grid_constant__ CUtensorMap zmap, const __nv_bfloat16* __restrict__ U,
                      const __nv_bfloat16* __restrict__ sw, __nv_bfloat16* __restrict__ dx,
                      __nv_bfloat16* __restrict__ dz, float* __restrict__ dzp, int* __restrict__ grp_done,
-                     float* __restrict__ dUp, TileSplit sp, int T, int D, int R, int Rk, int residual) {
+                     float* __restrict__ dUp, float* __restrict__ dU_f32, __nv_bfloat16* __restrict__ dU,
+                     __nv_bfloat16* __restrict__ dsw, TileSplit sp, int T, int D, int R, int Rk, int residual) {
   using L = BwdSmem<W, RKP, NP>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = align_smem_1024(smem_raw);
@@ -508,7 +516,6 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
   const int j1 = (int)((int64_t)sp.n_tiles * (g + 1) / sp.n_groups);
   const int n = j1 - j0;
   const int d0 = dblk * kBD;
-  const bool has_static = sw != nullptr;
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < kBwdStages; ++s) {
@@ -535,47 +542,44 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
     prefetch_tensormap(&xmap);
     prefetch_tensormap(&zmap);
   }
-  // U block of this CTA's channels in smem (MMA-3 B operand), loaded once.
-  load_u_block<W, RKP>(smem + L::kOffU, U, sw, dblk, D, R, threadIdx.x, blockDim.x);
-  fence_proxy_async_smem();
-  if (warp == 1) {
-    tmem_alloc(&tmem_slot, L::kAlloc);
-    tmem_relinquish();
-  }
-  tc_fence_before();
-  __syncthreads();
-  tc_fence_after();
-  const uint32_t tmem = tmem_slot;
-  // U^T in TMEM (MMA-1 A operand): lane = channel, column c of tap w = ranks (2c, 2c+1).
-  if (warp >= kBwdCtl && ((warp - kBwdCtl) >> 2) == 0) {  // one warp per lane quarter
-    const int q = warp & 3, ch = q * 32 + lane, d = d0 + ch;
-#pragma unroll
-    for (int w = 0; w < W; ++w) {
-#pragma unroll
-      for (int c0 = 0; c0 < RKP / 2; c0 += 8) {
-        uint32_t v[8];
-#pragma unroll
-        for (int i = 0; i < 8; ++i) {
-          float f[2];
-#pragma unroll
-          for (int k2 = 0; k2 < 2; ++k2) {
-            const int r = 2 * (c0 + i) + k2;
-            f[k2] = 0.f;
-            if (d < D) {
-              if (r < R) f[k2] = __bfloat162float(U[((size_t)r * W + w) * D + d]);
-              else if (r == R && has_static) f[k2] = __bfloat162float(sw[(size_t)w * D + d]);
-            }
-          }
-          v[i] = pack_bf16x2(f[0], f[1]);
-        }
-        tmem_st8(tmem + ((uint32_t)(q * 32) << 16) + L::kColUA + w * (RKP / 2) + c0, v);
-      }
+  __syncthreads();  // barriers initialised: the producer starts its loads at once
+  uint32_t tmem = 0;
+  if (warp != 0) {
+    // Everything but the producer: U block of this CTA's channels in smem (MMA-3 B
+    // operand; ranks >= R zero, rank R = static_w), TMEM allocation, then U^T in
+    // TMEM (MMA-1 A operand: lane = channel, column c of tap w = ranks (2c, 2c+1),
+    // which are adjacent in the K-major smem copy).
+    constexpr int kNonProducer = kBwdThreads - 32;
+    load_u_block<W, RKP>(smem + L::kOffU, U, sw, dblk, D, R, threadIdx.x - 32, kNonProducer);
+    fence_proxy_async_smem();
+    if (warp == 1) {
+      tmem_alloc(&tmem_slot, L::kAlloc);
+      tmem_relinquish();
     }
-    tmem_st_wait();
+    tc_fence_before();
+    named_bar_sync(2, kNonProducer);
+    tc_fence_after();
+    tmem = tmem_slot;
+    if (warp >= kBwdCtl && ((warp - kBwdCtl) >> 2) == 0) {  // one warp per lane quarter
+      const int q = warp & 3, ch = q * 32 + lane;
+      const uint8_t* us = smem + L::kOffU;
+#pragma unroll
+      for (int w = 0; w < W; ++w) {
+#pragma unroll
+        for (int c0 = 0; c0 < RKP / 2; c0 += 8) {
+          uint32_t v[8];
+#pragma unroll
+          for (int i = 0; i < 8; ++i)
+            v[i] = *reinterpret_cast<const uint32_t*>(us + w * L::kUTap + kmajor_off(ch, 2 * (c0 + i), L::kUChunk, 128));
+          tmem_st8(tmem + ((uint32_t)(q * 32) << 16) + L::kColUA + w * (RKP / 2) + c0, v);
+        }
+      }
+      tmem_st_wait();
+    }
+    tc_fence_before();
+    named_bar_sync(2, kNonProducer);
+    tc_fence_after();
   }
-  tc_fence_before();
-  __syncthreads();
-  tc_fence_after();
 
   if (warp == 0) {
     // ------------------------------------------------------------ producer
@@ -774,19 +778,17 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
     // dU partial of this CTA: TMEM (lane = channel) -> dUp[g][r][w*D + d0 + ch]
     if (!dead) dead = !mbar_wait(&du_bar, 0, kErrWaitTail, &abort_flag);
     tc_fence_after();
-    if (!dead && pp == 0) {
+    if (!dead) {
+      // the four warps of a lane quarter split the W * RKP / 16 column chunks
+      for (int cidx = pp; cidx < W * (RKP / 16); cidx += 4) {
+        const int w = cidx / (RKP / 16), rc = cidx % (RKP / 16);
+        float v[16];
+        tmem_ld16(tmem + lane_base + L::kColDU + w * RKP + rc * 16, v);
+        tmem_ld_wait();
 #pragma unroll
-      for (int w = 0; w < W; ++w) {
-#pragma unroll
-        for (int rc = 0; rc < RKP / 16; ++rc) {
-          float v[16];
-          tmem_ld16(tmem + lane_base + L::kColDU + w * RKP + rc * 16, v);
-          tmem_ld_wait();
-#pragma unroll
-          for (int i = 0; i < 16; ++i) {
-            const int r = rc * 16 + i;
-            if (r < Rk && dok) dUp[((size_t)g * Rk + r) * W * D + (size_t)w * D + d0 + ch] = v[i];
-          }
+        for (int i = 0; i < 16; ++i) {
+          const int r = rc * 16 + i;
+          if (r < Rk && dok) dUp[((size_t)g * Rk + r) * W * D + (size_t)w * D + d0 + ch] = v[i];
         }
       }
     }
@@ -801,6 +803,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
   if (threadIdx.x == 0) {
     __threadfence();
     atomicAdd(&grp_done[g], 1);
+    atomicAdd(&grp_done[sp.n_groups], 1);  // grid-wide count, waited on before the dU reduction
     bool ok = !abort_flag;
     if (ok) {
       const volatile int* gd = grp_done + g;
@@ -845,6 +848,55 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
       }
     }
   }
+
+  // ---------------------------------------------------------------- dU reduction
+  // Every CTA published its dU partial with the counts above; once the whole grid
+  // has (cooperative launch: all CTAs are resident), CTA i sums its 1/grid slice of
+  // the [Rk][W*D] accumulator over the groups in group order (deterministic) and
+  // writes dU_f32, and the bf16 dU rows / dstatic_w row when they are requested.
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    bool ok = grp_ok != 0;
+    if (ok) {
+      const volatile int* gd = grp_done + sp.n_groups;
+      const uint64_t tstart = globaltimer_ns();
+      while (*gd < (int)gridDim.x) {
+        if (globaltimer_ns() - tstart > kWaitLimitNs) {
+          atomicCAS(&g_device_error, 0u, (unsigned)kErrWaitTail);
+          ok = false;
+          break;
+        }
+      }
+    }
+    __threadfence();
+    grp_ok = ok ? 1 : 0;
+  }
+  __syncthreads();
+  if (grp_ok) {
+    const int64_t wd = (int64_t)W * D;
+    const int64_t n4 = (int64_t)Rk * wd / 4;  // W*D % 4 == 0 (D % 8 == 0)
+    const int64_t lo = n4 * blockIdx.x / gridDim.x, hi = n4 * (blockIdx.x + 1) / gridDim.x;
+    for (int64_t i = lo + threadIdx.x; i < hi; i += blockDim.x) {
+      float4 a4 = make_float4(0.f, 0.f, 0.f, 0.f);
+      for (int gg = 0; gg < sp.n_groups; ++gg) {
+        const float4 f = __ldcg(reinterpret_cast<const float4*>(dUp) + (size_t)gg * n4 + i);
+        a4.x += f.x;
+        a4.y += f.y;
+        a4.z += f.z;
+        a4.w += f.w;
+      }
+      reinterpret_cast<float4*>(dU_f32)[i] = a4;
+      const int64_t e0 = 4 * i;
+      const int r = (int)(e0 / wd);
+      __nv_bfloat16* dst = r < R ? (dU ? dU + e0 : nullptr) : (dsw ? dsw + (e0 - (int64_t)R * wd) : nullptr);
+      if (dst) {
+        dst[0] = __float2bfloat16_rn(a4.x);
+        dst[1] = __float2bfloat16_rn(a4.y);
+        dst[2] = __float2bfloat16_rn(a4.z);
+        dst[3] = __float2bfloat16_rn(a4.w);
+      }
+    }
+  }
   tc_fence_before();
   __syncthreads();
   if (warp == 1) tmem_dealloc(tmem, L::kAlloc);
@@ -865,7 +917,7 @@ BwdWorkspace bwd_workspace(void* base, int64_t B, int64_t T, int64_t D, int Rk, 
   const int rkp = Rk <= 16 ? 16 : 32;
   BwdWorkspace w;
   const size_t dzp = al256((size_t)sp.n_dblk * sp.n_tiles * kBT * rkp * sizeof(float));
-  const size_t cnt = al256((size_t)sp.n_groups * sizeof(int));
+  const size_t cnt = al256((size_t)(sp.n_groups + 1) * sizeof(int));  // group counts + grid count
   const size_t dUp = al256((size_t)sp.n_groups * Rk * W * D * sizeof(float));
   const size_t zp = zpack_bytes(B, T, rkp);
   uint8_t* p = (uint8_t*)base;
@@ -892,7 +944,7 @@ int launch_bwd(const void* x, const void* z, const void* U, const void* sw, cons
   if ((s = make_btd_map(&xmap, x, B, T, D, kBD, kBT + W - 1))) return s;
   if ((s = make_zpack_map(&zmap, ws.zp, B, T, RKP, kZRows))) return s;
   if ((s = z_pack_launch(z, ws.zp, B, T, R, RKP, sw != nullptr, st))) return s;
-  cudaError_t e = cudaMemsetAsync(ws.cnt, 0, (size_t)sp.n_groups * sizeof(int), st);
+  cudaError_t e = cudaMemsetAsync(ws.cnt, 0, (size_t)(sp.n_groups + 1) * sizeof(int), st);
   if (e != cudaSuccess) return cuda_status(e, "cudaMemsetAsync(group counters)");
   const int smem = (int)L::kTotal;
   e = cudaFuncSetAttribute(lr_bwd_tc_kernel<W, RKP, NP>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
@@ -914,18 +966,14 @@ int launch_bwd(const void* x, const void* z, const void* U, const void* sw, cons
   cfg.attrs = attr;
   cfg.numAttrs = 1;
   e = cudaLaunchKernelEx(&cfg, lr_bwd_tc_kernel<W, RKP, NP>, dymap, xmap, zmap, (const __nv_bfloat16*)U,
-                         (const __nv_bfloat16*)sw, (__nv_bfloat16*)dx, (__nv_bfloat16*)dz, ws.dzp, ws.cnt, ws.dUp, sp,
-                         (int)T, (int)D, R, Rk, residual);
+                         (const __nv_bfloat16*)sw, (__nv_bfloat16*)dx, (__nv_bfloat16*)dz, ws.dzp, ws.cnt, ws.dUp,
+                         dU_f32, (__nv_bfloat16*)dU, (__nv_bfloat16*)(sw ? dsw : nullptr), sp, (int)T, (int)D, R, Rk,
+                         residual);
   if (e != cudaSuccess) {
     cudaGetLastError();
     return cuda_status(e, "cudaLaunchKernelEx(lr_bwd_tc_kernel)");
   }
   DYNCONV_CHECK_LAUNCH("lr_bwd_tc_kernel");
-  const int64_t nacc = (int64_t)Rk * W * D;
-  if ((s = reduce_partials_launch(ws.dUp, sp.n_groups, nacc, dU_f32, nullptr, DYNCONV_DTYPE_BF16, st))) return s;
-  if (dU && (s = cast_f32_launch(dU_f32, dU, (int64_t)R * W * D, DYNCONV_DTYPE_BF16, st))) return s;
-  if (sw && dsw && (s = cast_f32_launch(dU_f32 + (int64_t)R * W * D, dsw, (int64_t)W * D, DYNCONV_DTYPE_BF16, st)))
-    return s;
   return DYNCONV_OK;
 }
 
