@@ -197,6 +197,21 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
   return ok != 0;
 }
 
+// As mbar_try_wait, but the thread may be suspended for up to `suspend_ns` while
+// the phase is incomplete (it resumes as soon as the phase completes), so a waiting
+// warp does not spend issue slots spinning.
+__device__ __forceinline__ bool mbar_try_wait_suspend(uint64_t* bar, uint32_t parity, uint32_t suspend_ns) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.acquire.cta.shared::cta.b64 p, [%1], %2, %3;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity), "r"(suspend_ns)
+      : "memory");
+  return ok != 0;
+}
+
 __device__ __forceinline__ uint64_t globaltimer_ns() {
   uint64_t t;
   asm volatile("mov.u64 %0, %globaltimer;" : "=l"(t));
@@ -208,18 +223,17 @@ __device__ __forceinline__ uint64_t globaltimer_ns() {
 // `site` in g_device_error, raises the CTA's abort flag and returns false, so the
 // kernel unwinds instead of hanging the GPU.
 constexpr uint64_t kWaitLimitNs = 1500000000ull;  // 1.5 s
+constexpr uint32_t kWaitSuspendNs = 1000000u;       // longest single suspension, 1 ms
 
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, unsigned int site,
                                           volatile int* abort_flag) {
   if (mbar_try_wait(bar, parity)) return true;  // fast path: phase already complete
   if (*abort_flag) return false;
   const uint64_t t0 = globaltimer_ns();
-  for (uint32_t i = 1;; ++i) {
-    if (mbar_try_wait(bar, parity)) return true;
-    if ((i & 255u) == 0) {
-      if (*abort_flag) return false;
-      if (globaltimer_ns() - t0 > kWaitLimitNs) break;
-    }
+  for (;;) {
+    if (mbar_try_wait_suspend(bar, parity, kWaitSuspendNs)) return true;
+    if (*abort_flag) return false;
+    if (globaltimer_ns() - t0 > kWaitLimitNs) break;
   }
   atomicCAS(&g_device_error, 0u, site);
   *abort_flag = 1;

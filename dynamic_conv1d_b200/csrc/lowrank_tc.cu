@@ -16,11 +16,12 @@
 //        -> TMEM acc_w[ch][t] = sum_r U[r,w,ch] z[t,r]      (the dynamic weights;
 //                                                            never written to HBM)
 //   epilogue warps: y[t,ch] = sum_w acc_w[ch][t] * x[t-w,ch] (+ x[t,ch])
-//        -> per-warp smem y sub-tile [32 steps][32 ch] -> TMA store issued by the warp
+//        -> per-warp smem y sub-tile [16 steps][32 ch] -> TMA store issued by the warp
 //
-// Warp roles (320 threads, one CTA per SM, persistent over a contiguous range
+// Warp roles (576 threads, one CTA per SM, persistent over a contiguous range
 // of work items):  warp 0 producer, warp 1 TMEM owner + MMA issuer (one lane),
-// warps 2..9 epilogue (two warps per TMEM lane quarter, one per 32-step half).
+// warps 2..17 epilogue (four warps per TMEM lane quarter, one per 16-step quarter
+// of the tile).
 // Pipelines: S-stage x/z ring (full/empty mbarriers), double-buffered TMEM
 // accumulators (acc_full via tcgen05.commit / acc_empty), a double-buffered y
 // sub-tile per epilogue warp (the warp's own TMA store bulk groups), so the
@@ -42,7 +43,8 @@ namespace {
 constexpr int kBT = 64;         // timesteps per work item (MMA N)
 constexpr int kBD = 128;        // channels per work item (MMA M)
 constexpr int kStages = 4;      // x/z pipeline depth (forward, R_kernel <= 32)
-constexpr int kEpiWarps = 8;    // epilogue warps
+constexpr int kEpiWarps = 16;   // forward epilogue warps: four per TMEM lane quarter
+constexpr int kEpiSteps = kBT / (kEpiWarps / 4);  // timesteps per epilogue warp and tile
 constexpr int kFwdThreads = 64 + 32 * kEpiWarps;
 
 
@@ -159,7 +161,7 @@ struct FwdSmem {
   static constexpr uint32_t kXBytes = (uint32_t)kXRows * kBD * 2;        // TMA box bytes
   static constexpr uint32_t kXStride = (kXBytes + 1023u) / 1024u * 1024u;
   static constexpr uint32_t kZBytes = (uint32_t)kBT * RKP * 2;           // K-major, 64 rows x RKP
-  static constexpr uint32_t kYWarpBytes = 32 * 32 * 2;  // one epilogue warp's y sub-tile [32 steps][32 ch]
+  static constexpr uint32_t kYWarpBytes = kEpiSteps * 32 * 2;  // one epilogue warp's y sub-tile [steps][32 ch]
   static constexpr uint32_t kUTap = (uint32_t)kBD * RKP * 2;
   static constexpr uint32_t kOffX = 0;
   static constexpr uint32_t kOffZ = kOffX + kS * kXStride;
@@ -174,29 +176,46 @@ struct FwdSmem {
 };
 
 // Loads U_ext for channel block dblk into smem: one [128 ch x RKP] K-major block per
-// tap (rank R = static_w when present, zero padding up to RKP).  All `nthreads`
-// threads take part; each reads 16-byte vectors (8 channels of one (rank, tap) row;
-// D % 8 == 0 on this path, so a vector never straddles the end of D).
-template <int W, int RKP>
+// tap (rank R = static_w when present, zero padding up to RKP).  The NT calling
+// threads each read up to ceil(W*RKP*16 / NT) 16-byte vectors (8 channels of one
+// (rank, tap) row; D % 8 == 0 on this path, so a vector never straddles the end
+// of D), all loads issued before any store so their latencies overlap.
+template <int W, int RKP, int NT>
 __device__ void load_u_block(uint8_t* us, const __nv_bfloat16* __restrict__ U, const __nv_bfloat16* __restrict__ sw,
-                             int dblk, int D, int R, int tid, int nthreads) {
+                             int dblk, int D, int R, int tid) {
   constexpr uint32_t kUTap = (uint32_t)kBD * RKP * 2;
   constexpr uint32_t kUSbo = (RKP / 8) * 128;
+  constexpr int NV = W * RKP * (kBD / 8);
+  constexpr int PER = (NV + NT - 1) / NT;
   const int d0 = dblk * kBD;
-  for (int e = tid; e < W * RKP * (kBD / 8); e += nthreads) {
-    const int v8 = e % (kBD / 8);  // 8-channel group
-    const int r = (e / (kBD / 8)) % RKP;
-    const int w = e / ((kBD / 8) * RKP);
-    const int d = d0 + v8 * 8;
-    uint4 u = make_uint4(0, 0, 0, 0);
-    if (d < D) {
-      if (r < R) u = __ldg(reinterpret_cast<const uint4*>(U + ((size_t)r * W + w) * D + d));
-      else if (r == R && sw != nullptr) u = __ldg(reinterpret_cast<const uint4*>(sw + (size_t)w * D + d));
-    }
-    const __nv_bfloat16* h = reinterpret_cast<const __nv_bfloat16*>(&u);
+  uint4 u[PER];
 #pragma unroll
-    for (int i = 0; i < 8; ++i)
-      *reinterpret_cast<__nv_bfloat16*>(us + w * kUTap + kmajor_off(v8 * 8 + i, r, kUSbo, 128)) = h[i];
+  for (int i = 0; i < PER; ++i) {
+    const int e = tid + i * NT;
+    u[i] = make_uint4(0, 0, 0, 0);
+    if (e < NV) {
+      const int v8 = e % (kBD / 8);  // 8-channel group
+      const int r = (e / (kBD / 8)) % RKP;
+      const int w = e / ((kBD / 8) * RKP);
+      const int d = d0 + v8 * 8;
+      if (d < D) {
+        if (r < R) u[i] = __ldg(reinterpret_cast<const uint4*>(U + ((size_t)r * W + w) * D + d));
+        else if (r == R && sw != nullptr) u[i] = __ldg(reinterpret_cast<const uint4*>(sw + (size_t)w * D + d));
+      }
+    }
+  }
+#pragma unroll
+  for (int i = 0; i < PER; ++i) {
+    const int e = tid + i * NT;
+    if (e < NV) {
+      const int v8 = e % (kBD / 8);
+      const int r = (e / (kBD / 8)) % RKP;
+      const int w = e / ((kBD / 8) * RKP);
+      const __nv_bfloat16* h = reinterpret_cast<const __nv_bfloat16*>(&u[i]);
+#pragma unroll
+      for (int k = 0; k < 8; ++k)
+        *reinterpret_cast<__nv_bfloat16*>(us + w * kUTap + kmajor_off(v8 * 8 + k, r, kUSbo, 128)) = h[k];
+    }
   }
 }
 
@@ -247,7 +266,7 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
     // U block of this CTA's channels (MMA A operand), loaded once by all but the
     // producer, then the TMEM allocation.
     constexpr int kNonProducer = kFwdThreads - 32;
-    load_u_block<W, RKP>(smem + L::kOffU, U, sw, dblk, D, R, threadIdx.x - 32, kNonProducer);
+    load_u_block<W, RKP, kNonProducer>(smem + L::kOffU, U, sw, dblk, D, R, threadIdx.x - 32);
     fence_proxy_async_smem();
     if (warp == 1) {
       tmem_alloc(&tmem_slot, kTmemCols);
@@ -300,9 +319,9 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
     }
   } else {
     // ------------------------------------------------------------ epilogue
-    const int e = warp - 2;            // 0..7
+    const int e = warp - 2;            // 0..kEpiWarps-1
     const int q = warp & 3;            // TMEM lane quarter this warp may access
-    const int half = e >> 2;           // which 32-step half of the tile
+    const int part = e >> 2;           // which kEpiSteps-step part of the tile
     const int ch = q * 32 + lane;      // channel within the block (= TMEM lane)
     const uint64_t pol_y = policy_evict_first();
     bool dead = false;  // a bounded wait gave up: skip the work, keep arriving
@@ -320,11 +339,11 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
         const __nv_bfloat16* xs = reinterpret_cast<const __nv_bfloat16*>(smem + L::kOffX + s * L::kXStride);
         // x window: xr[j] = x at step (tok0 - (W-1) + j); smem row of step t is (t - t0) + (W-1)
         float xr[16 + W - 1];
-        const int tok0 = half * 32;
+        const int tok0 = part * kEpiSteps;
 #pragma unroll
         for (int j = 0; j < W - 1; ++j) xr[j] = __bfloat162float(xs[(tok0 + j) * kBD + ch]);
 #pragma unroll
-        for (int c = 0; c < 2; ++c) {
+        for (int c = 0; c < kEpiSteps / 16; ++c) {
           const int tb = tok0 + c * 16;
           float acc[W][16];
 #pragma unroll
@@ -352,7 +371,7 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
         mbar_arrive(&acce_bar[a]);
         mbar_arrive(&empty_bar[s]);
         if (!dead) {
-          tma_store_3d(&ymap, ys, d0 + q * 32, t0 + half * 32, b, pol_y);
+          tma_store_3d(&ymap, ys, d0 + q * 32, t0 + part * kEpiSteps, b, pol_y);
           bulk_commit_group();
         }
       }
@@ -373,7 +392,7 @@ int launch_fwd(const void* x, const void* z, const void* U, const void* sw, void
   CUtensorMap xmap, ymap, zmap;
   int s;
   if ((s = make_btd_map(&xmap, x, B, T, D, kBD, kBT + W - 1))) return s;
-  if ((s = make_btd_map(&ymap, y, B, T, D, 32, 32))) return s;  // per-warp [32 steps][32 ch] stores
+  if ((s = make_btd_map(&ymap, y, B, T, D, 32, kEpiSteps))) return s;  // per-warp [steps][32 ch] stores
   if ((s = make_zpack_map(&zmap, ws, B, T, RKP, kBT))) return s;
   if ((s = z_pack_launch(z, ws, B, T, R, RKP, sw != nullptr, st))) return s;
   const TileSplit sp = tile_split(B, T, D);
@@ -550,7 +569,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
     // TMEM (MMA-1 A operand: lane = channel, column c of tap w = ranks (2c, 2c+1),
     // which are adjacent in the K-major smem copy).
     constexpr int kNonProducer = kBwdThreads - 32;
-    load_u_block<W, RKP>(smem + L::kOffU, U, sw, dblk, D, R, threadIdx.x - 32, kNonProducer);
+    load_u_block<W, RKP, kNonProducer>(smem + L::kOffU, U, sw, dblk, D, R, threadIdx.x - 32);
     fence_proxy_async_smem();
     if (warp == 1) {
       tmem_alloc(&tmem_slot, L::kAlloc);
