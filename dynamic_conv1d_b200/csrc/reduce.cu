@@ -10,33 +10,25 @@
 namespace dynconv {
 
 // out_f32[i] = sum_p part[p*n + i] (p ascending); optionally also cast into out (dtype T).
+// One element per thread; the partial rows are loaded eight at a time ahead of the
+// (still ascending) additions, so the load latencies overlap.
 template <typename T>
 __global__ void __launch_bounds__(256) reduce_partials_kernel(const float* __restrict__ part, int P, int64_t n,
                                                               float* __restrict__ out_f32, T* __restrict__ out) {
-  const int64_t stride = (int64_t)gridDim.x * blockDim.x * 4;
-  for (int64_t i0 = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) * 4; i0 < n; i0 += stride) {
-    float acc[4] = {0.f, 0.f, 0.f, 0.f};
-    if (i0 + 4 <= n && (n & 3) == 0) {
-      for (int p = 0; p < P; ++p) {
-        const float4 v = __ldg(reinterpret_cast<const float4*>(part + (int64_t)p * n + i0));
-        acc[0] += v.x;
-        acc[1] += v.y;
-        acc[2] += v.z;
-        acc[3] += v.w;
-      }
+  constexpr int kAhead = 8;
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x) {
+    float acc = 0.f;
+    int p = 0;
+    for (; p + kAhead <= P; p += kAhead) {
+      float v[kAhead];
 #pragma unroll
-      for (int j = 0; j < 4; ++j) {
-        if (out_f32) out_f32[i0 + j] = acc[j];
-        if (out) out[i0 + j] = Elem<T>::from_f(acc[j]);
-      }
-    } else {
-      for (int j = 0; j < 4 && i0 + j < n; ++j) {
-        float a = 0.f;
-        for (int p = 0; p < P; ++p) a += part[(int64_t)p * n + i0 + j];
-        if (out_f32) out_f32[i0 + j] = a;
-        if (out) out[i0 + j] = Elem<T>::from_f(a);
-      }
+      for (int j = 0; j < kAhead; ++j) v[j] = __ldg(part + (int64_t)(p + j) * n + i);
+#pragma unroll
+      for (int j = 0; j < kAhead; ++j) acc += v[j];
     }
+    for (; p < P; ++p) acc += __ldg(part + (int64_t)p * n + i);
+    if (out_f32) out_f32[i] = acc;
+    if (out) out[i] = Elem<T>::from_f(acc);
   }
 }
 
@@ -47,7 +39,7 @@ __global__ void __launch_bounds__(256) cast_f32_kernel(const float* __restrict__
 }
 
 static unsigned reduce_grid(int64_t n) {
-  int64_t g = (n / 4 + 255) / 256;
+  int64_t g = (n + 255) / 256;
   const int64_t cap = (int64_t)sm_count() * 8;
   if (g > cap) g = cap;
   if (g < 1) g = 1;
