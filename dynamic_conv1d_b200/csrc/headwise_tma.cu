@@ -125,6 +125,39 @@ __device__ __forceinline__ VecT packv2(const float2 (&f)[kVec / 2]) {
   return u;
 }
 
+// Lane-to-channel maps.  Default: lane l owns channels 4l..4l+3 of the 128-channel
+// block (one 8-byte vector).  SPLIT (head_size 1 only): lane l owns channels
+// 2l, 2l+1, 64+2l, 65+2l, so that its heads' weights (2 heads x W taps per pair)
+// sit at a 16-byte lane stride in shared memory -- the 32-byte stride of the
+// default map makes those reads 2-way bank-conflicted.
+template <bool SPLIT>
+__device__ __forceinline__ int lane_ch(int lane, int c) {
+  return SPLIT ? ((c >> 1) * 64 + 2 * lane + (c & 1)) : (kVec * lane + c);
+}
+
+// The lane's kVec channels of one row (row = first channel of the block).
+template <bool SPLIT>
+__device__ __forceinline__ VecT ld_lane(const __nv_bfloat16* row, int lane) {
+  if constexpr (SPLIT) {
+    VecT v;
+    v.x = *reinterpret_cast<const uint32_t*>(row + 2 * lane);
+    v.y = *reinterpret_cast<const uint32_t*>(row + 64 + 2 * lane);
+    return v;
+  } else {
+    return *reinterpret_cast<const VecT*>(row + kVec * lane);
+  }
+}
+
+template <bool SPLIT>
+__device__ __forceinline__ void st_lane(__nv_bfloat16* row, int lane, VecT v) {
+  if constexpr (SPLIT) {
+    *reinterpret_cast<uint32_t*>(row + 2 * lane) = v.x;
+    *reinterpret_cast<uint32_t*>(row + 64 + 2 * lane) = v.y;
+  } else {
+    *reinterpret_cast<VecT*>(row + kVec * lane) = v;
+  }
+}
+
 // Packed fp32 pair arithmetic (sm_100 f32x2 instructions, round to nearest even).
 __device__ __forceinline__ float2 fma2(float2 a, float2 b, float2 c) {
   float2 d;
@@ -217,13 +250,18 @@ __device__ __forceinline__ void head_reduce_store(float (&v)[W], int lane, int l
 
 // Weights of the thread's heads for one row: wt[j][w] for the head of channel
 // group j (j < HPT; HPT = 1 when the lane's channels share one head).
-template <int K, int W>
+template <int K, int W, bool SPLIT>
 __device__ __forceinline__ void load_row_weights(const __nv_bfloat16* wrow, int lane, int log2hs,
                                                  float (&wt)[kVec / K][W]) {
   constexpr int HPT = kVec / K;
   constexpr int N = HPT * W;
   __align__(16) __nv_bfloat16 v[N];
-  if constexpr (K == kVec) {
+  if constexpr (SPLIT) {  // K == 1: heads 2l, 2l+1 and 64+2l, 65+2l
+    __nv_bfloat16(&lo)[2 * W] = *reinterpret_cast<__nv_bfloat16(*)[2 * W]>(v);
+    __nv_bfloat16(&hi)[2 * W] = *reinterpret_cast<__nv_bfloat16(*)[2 * W]>(v + 2 * W);
+    ld_bf16<2 * W, pow2_align(4 * W)>(wrow + 2 * lane * W, lo);
+    ld_bf16<2 * W, pow2_align(4 * W)>(wrow + (64 + 2 * lane) * W, hi);
+  } else if constexpr (K == kVec) {
     const int hl = (kVec * lane) >> log2hs;  // local head of the block
     ld_bf16<N, pow2_align(2 * W)>(wrow + hl * W, v);
   } else {
@@ -235,7 +273,7 @@ __device__ __forceinline__ void load_row_weights(const __nv_bfloat16* wrow, int 
     for (int w = 0; w < W; ++w) wt[j][w] = __bfloat162float(v[j * W + w]);
 }
 
-template <int K, int W, bool BWD>
+template <int K, int W, bool BWD, bool SPLIT>
 __global__ void __launch_bounds__(kHwThreads, kCtasPerSm)
     hw_tma_kernel(const __grid_constant__ CUtensorMap xmap, const __grid_constant__ CUtensorMap dymap,
                   const __grid_constant__ CUtensorMap wmap, const __nv_bfloat16* __restrict__ sw,
@@ -299,14 +337,14 @@ __global__ void __launch_bounds__(kHwThreads, kCtasPerSm)
   // Channel pairs (c = 2p, 2p+1) are computed with packed fp32 instructions
   // (fma/add/mul .rn.f32x2): each lane of a pair rounds exactly like the scalar op.
   constexpr int P = kVec / 2;
-  const int dch = d0 + kVec * lane;
+  const int dch = d0 + lane_ch<SPLIT>(lane, 0);  // first channel of the lane (SPLIT: D % 128 == 0)
   const bool dok = dch < D;
   const int r0 = warp * RPT;
   float2 s2[W][P];
 #pragma unroll
   for (int w = 0; w < W; ++w) {
     if (sw != nullptr && dok) {
-      unpackv2(*reinterpret_cast<const VecT*>(sw + (size_t)w * D + dch), s2[w]);
+      unpackv2(ld_lane<SPLIT>(sw + (size_t)w * D + d0, lane), s2[w]);
     } else {
 #pragma unroll
       for (int q = 0; q < P; ++q) s2[w][q] = make_float2(0.f, 0.f);
@@ -328,19 +366,19 @@ __global__ void __launch_bounds__(kHwThreads, kCtasPerSm)
       break;
     }
     const uint8_t* st = smem + s * G::STAGE;
-    const __nv_bfloat16* xs = reinterpret_cast<const __nv_bfloat16*>(st) + kVec * lane;
+    const __nv_bfloat16* xs = reinterpret_cast<const __nv_bfloat16*>(st);
     const __nv_bfloat16* ws = reinterpret_cast<const __nv_bfloat16*>(st + G::X_BYTES + G::DY_BYTES);
 
     if constexpr (!BWD) {
       // x rows r0 .. r0+RPT+W-2 of the tile (step t0 - (W-1) + i)
       float2 xr[RPT + W - 1][P];
 #pragma unroll
-      for (int i = 0; i < RPT + W - 1; ++i) unpackv2(*reinterpret_cast<const VecT*>(xs + (r0 + i) * kCB), xr[i]);
+      for (int i = 0; i < RPT + W - 1; ++i) unpackv2(ld_lane<SPLIT>(xs + (r0 + i) * kCB, lane), xr[i]);
 #pragma unroll
       for (int rr = 0; rr < RPT; ++rr) {
         const int t = t0 + r0 + rr;
         float wt[HPT][W];
-        load_row_weights<K, W>(ws + (r0 + rr) * wb, lane, log2hs, wt);
+        load_row_weights<K, W, SPLIT>(ws + (r0 + rr) * wb, lane, log2hs, wt);
         float2 y[P];
 #pragma unroll
         for (int q = 0; q < P; ++q) {
@@ -351,16 +389,16 @@ __global__ void __launch_bounds__(kHwThreads, kCtasPerSm)
             y[q] = fma2(coef, xr[rr + W - 1 - w][q], y[q]);
           }
         }
-        if (dok && t < T) *reinterpret_cast<VecT*>(out + ((size_t)b * T + t) * D + dch) = packv2(y);
+        if (dok && t < T) st_lane<SPLIT>(out + ((size_t)b * T + t) * D + d0, lane, packv2(y));
       }
     } else {
-      const __nv_bfloat16* dys = reinterpret_cast<const __nv_bfloat16*>(st + G::X_BYTES) + kVec * lane;
+      const __nv_bfloat16* dys = reinterpret_cast<const __nv_bfloat16*>(st + G::X_BYTES);
       // dy rows r0 .. r0+RPT+W-2 (step t0 + i); x rows r0 .. r0+RPT+W-2 (step t0 - (W-1) + i)
       float2 dyf[RPT + W - 1][P], xf[RPT + W - 1][P];
 #pragma unroll
       for (int i = 0; i < RPT + W - 1; ++i) {
-        unpackv2(*reinterpret_cast<const VecT*>(dys + (r0 + i) * kCB), dyf[i]);
-        unpackv2(*reinterpret_cast<const VecT*>(xs + (r0 + i) * kCB), xf[i]);
+        unpackv2(ld_lane<SPLIT>(dys + (r0 + i) * kCB, lane), dyf[i]);
+        unpackv2(ld_lane<SPLIT>(xs + (r0 + i) * kCB, lane), xf[i]);
       }
       // dx[t] = sum_w (weight[t+w, h, w] + static_w[w]) * dy[t+w]  (+ dy[t]).  Weight row
       // j (step t0 + r0 + j) is read once and feeds dx rows j - w.
@@ -372,7 +410,7 @@ __global__ void __launch_bounds__(kHwThreads, kCtasPerSm)
 #pragma unroll
       for (int j = 0; j < RPT + W - 1; ++j) {
         float wt[HPT][W];
-        load_row_weights<K, W>(ws + (r0 + j) * wb, lane, log2hs, wt);
+        load_row_weights<K, W, SPLIT>(ws + (r0 + j) * wb, lane, log2hs, wt);
 #pragma unroll
         for (int w = 0; w < W; ++w) {
           const int rr = j - w;
@@ -389,7 +427,7 @@ __global__ void __launch_bounds__(kHwThreads, kCtasPerSm)
       for (int rr = 0; rr < RPT; ++rr) {
         const int t = t0 + r0 + rr;
         const bool row_ok = dok && t < T;
-        if (row_ok) *reinterpret_cast<VecT*>(out + ((size_t)b * T + t) * D + dch) = packv2(dxv[rr]);
+        if (row_ok) st_lane<SPLIT>(out + ((size_t)b * T + t) * D + d0, lane, packv2(dxv[rr]));
         // P_w = dy[t] * x[t-w]: dstatic_w (per channel, fused multiply-add) and
         // dweight (summed over the head's channels)
 #pragma unroll
@@ -423,7 +461,17 @@ __global__ void __launch_bounds__(kHwThreads, kCtasPerSm)
                 v[q * W + w] = __float2bfloat16_rn(pr.x + pr.y);
               }
             }
-          if (row_ok) st_bf16<HPT * W, pow2_align(2 * HPT * W)>(dw + (((size_t)b * T + t) * H + dch / K) * W, v);
+          if (row_ok) {
+            __nv_bfloat16* drow = dw + ((size_t)b * T + t) * H * W;
+            if constexpr (SPLIT) {
+              __nv_bfloat16(&lo)[2 * W] = *reinterpret_cast<__nv_bfloat16(*)[2 * W]>(v);
+              __nv_bfloat16(&hi)[2 * W] = *reinterpret_cast<__nv_bfloat16(*)[2 * W]>(v + 2 * W);
+              st_bf16<2 * W, pow2_align(4 * W)>(drow + (size_t)(d0 + 2 * lane) * W, lo);
+              st_bf16<2 * W, pow2_align(4 * W)>(drow + (size_t)(d0 + 64 + 2 * lane) * W, hi);
+            } else {
+              st_bf16<HPT * W, pow2_align(2 * HPT * W)>(drow + (size_t)(dch / K) * W, v);
+            }
+          }
         }
       }
     }
@@ -447,8 +495,8 @@ __global__ void __launch_bounds__(kHwThreads, kCtasPerSm)
       for (int w = 0; w < W; ++w)
 #pragma unroll
         for (int q = 0; q < P; ++q) {
-          red[(warp * W + w) * kCB + kVec * lane + 2 * q] = acc_sw[w][q].x;
-          red[(warp * W + w) * kCB + kVec * lane + 2 * q + 1] = acc_sw[w][q].y;
+          red[(warp * W + w) * kCB + lane_ch<SPLIT>(lane, 2 * q)] = acc_sw[w][q].x;
+          red[(warp * W + w) * kCB + lane_ch<SPLIT>(lane, 2 * q + 1)] = acc_sw[w][q].y;
         }
       named_bar_sync(1, kNC * 32);
       for (int i = threadIdx.x; i < W * kCB; i += kNC * 32) {
@@ -476,7 +524,7 @@ HwSplit hw_split(int64_t B, int64_t T, int64_t D, int TR) {
 
 int hw_tr(int K, bool bwd) { return bwd ? 16 : (K == kVec ? 64 : 16); }
 
-template <int K, int W, bool BWD>
+template <int K, int W, bool BWD, bool SPLIT>
 int launch_hw_tma(const void* x, const void* wgt, const void* sw, const void* dy, void* out, void* dw, float* part,
                   int64_t B, int64_t T, int64_t D, int64_t H, int log2hs, int residual, cudaStream_t st) {
   using G = HwGeo<K, W, BWD>;
@@ -512,7 +560,7 @@ int launch_hw_tma(const void* x, const void* wgt, const void* sw, const void* dy
     const cuuint32_t box[4] = {128, (cuuint32_t)wchunks, (cuuint32_t)G::ROWS_A, 1};
     if ((s = encode_tensor_map_bf16(&wmap, wgt, 4, dims, strides, box))) return s;
   }
-  auto kern = hw_tma_kernel<K, W, BWD>;
+  auto kern = hw_tma_kernel<K, W, BWD, SPLIT>;
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, G::SMEM);
   if (e != cudaSuccess) {
     cudaGetLastError();
@@ -531,8 +579,11 @@ int hw_tma_dispatch(const void* x, const void* wgt, const void* sw, const void* 
                     int64_t B, int64_t T, int64_t D, int64_t H, int W, int log2hs, int residual, cudaStream_t st) {
   const int K = log2hs >= 2 ? 4 : (1 << log2hs);
 #define DYNCONV_HWT(KK, WW)                                                                                       \
-  if (K == KK && W == WW)                                                                                         \
-    return launch_hw_tma<KK, WW, BWD>(x, wgt, sw, dy, out, dw, part, B, T, D, H, log2hs, residual, st);
+  if (K == KK && W == WW) {                                                                                       \
+    if (KK == 1 && D % kCB == 0)                                                                                  \
+      return launch_hw_tma<KK, WW, BWD, KK == 1>(x, wgt, sw, dy, out, dw, part, B, T, D, H, log2hs, residual, st); \
+    return launch_hw_tma<KK, WW, BWD, false>(x, wgt, sw, dy, out, dw, part, B, T, D, H, log2hs, residual, st);     \
+  }
   DYNCONV_HWT(1, 1) DYNCONV_HWT(1, 2) DYNCONV_HWT(1, 3) DYNCONV_HWT(1, 4)
   DYNCONV_HWT(2, 1) DYNCONV_HWT(2, 2) DYNCONV_HWT(2, 3) DYNCONV_HWT(2, 4)
   DYNCONV_HWT(4, 1) DYNCONV_HWT(4, 2) DYNCONV_HWT(4, 3) DYNCONV_HWT(4, 4)
