@@ -307,7 +307,7 @@ def run_ours(args, wl: dict) -> None:
     if world > 1:
         from datetime import timedelta
 
-        dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=dev)
+        dist.init_process_group("nccl", timeout=timedelta(seconds=60), device_id=dev)
 
     B, T, D, W = wl["B"], wl["T"], wl["D"], wl["W"]
     ntok = B * T
@@ -407,9 +407,19 @@ def run_ours(args, wl: dict) -> None:
         # The timed region is a few milliseconds, shorter than the 200 ms sampling
         # period: keep the same step running (untimed) until the sampler has seen
         # at least 3 samples under this load.
+        # Every replay holds the data-parallel all-reduce, so all ranks must run
+        # the same number of them: each round the ranks agree (MAX) on whether any
+        # of them still needs samples.
         clk.mark()
         t_end = time.perf_counter() + 5.0
-        while clk.samples_since_mark() < 3 and time.perf_counter() < t_end:
+        while True:
+            need = clk.samples_since_mark() < 3 and time.perf_counter() < t_end
+            if world > 1:
+                flag = torch.tensor([1 if need else 0], device=dev, dtype=torch.int32)
+                dist.all_reduce(flag, op=dist.ReduceOp.MAX)
+                need = bool(flag.item())
+            if not need:
+                break
             for _ in range(20):
                 flush.zero_()
                 run_one()
