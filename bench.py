@@ -19,7 +19,8 @@ Reported (one JSON line on rank 0):
               replayed from a CUDA graph so host overhead is not measured;
   e2e         the same metric through the public autograd API with the step's
               inputs (x, z, dy) copied from pinned host memory and all results
-              (y, dx, dz, dU, dstatic_w) copied back, inside the timed region;
+              (y, dx, dz, dU, dstatic_w) copied back, inside the timed region
+              (pipelined over batch rows so uploads and downloads overlap);
   roofline    the dominant kernel (the lowrank backward call) -- algorithmic bytes
               per launch / its CUDA-event duration, against MEASURED_PEAKS.json;
   cpu_baseline the numpy oracle (a restatement of the reference's reference.py) on
@@ -596,7 +597,12 @@ def ctypes_stream(st):
 
 def end_to_end(args, wl, a, a_sw, fn, dev, world, dp_ctx) -> dict:
     """Public API with pinned host buffers: H2D of x, z/weight, dy; fwd+bwd; D2H of
-    y and every gradient; all inside the CUDA-event-timed region."""
+    y and every gradient; all inside the CUDA-event-timed region.
+
+    The step is pipelined over batch rows on three streams -- uploads of row i+1
+    and downloads of row i-1 overlap the fwd+bwd of row i (PCIe is full duplex) --
+    and the shared gradients (dU, dstatic_w) accumulate over the rows as autograd
+    does for any split batch; they are copied back once per step."""
     import torch
 
     bf = torch.bfloat16
@@ -615,34 +621,52 @@ def end_to_end(args, wl, a, a_sw, fn, dev, world, dp_ctx) -> dict:
     h2d = sum(t.numel() * t.element_size() for t in host.values())
     d2h = sum(t.numel() * t.element_size() for t in outs.values())
     res = bool(wl["residual"])
+    comp = torch.cuda.current_stream(dev)
+    s_in, s_out = torch.cuda.Stream(device=dev), torch.cuda.Stream(device=dev)
+    rows = wl["B"]
 
     def step():
-        x = host["x"].to(dev, non_blocking=True).requires_grad_()
-        s2 = host[second].to(dev, non_blocking=True).requires_grad_()
-        dy = host["dy"].to(dev, non_blocking=True)
         if U is not None:
             U.grad = None
         sw.grad = None
-        args_ = [x, s2, U, sw] if U is not None else [x, s2, sw]
-        with dp_ctx():
-            y = fn(*args_, residual=res)
-            y.backward(dy)
-        outs["y"].copy_(y.detach(), non_blocking=True)
-        outs["dx"].copy_(x.grad, non_blocking=True)
-        outs["d2"].copy_(s2.grad, non_blocking=True)
-        outs["dsw"].copy_(sw.grad, non_blocking=True)
-        if U is not None:
-            outs["dU"].copy_(U.grad, non_blocking=True)
+        for r in range(rows):
+            sl = slice(r, r + 1)
+            with torch.cuda.stream(s_in):
+                x = host["x"][sl].to(dev, non_blocking=True)
+                s2 = host[second][sl].to(dev, non_blocking=True)
+                dy = host["dy"][sl].to(dev, non_blocking=True)
+            comp.wait_stream(s_in)
+            for t in (x, s2, dy):
+                t.record_stream(comp)
+            x.requires_grad_()
+            s2.requires_grad_()
+            args_ = [x, s2, U, sw] if U is not None else [x, s2, sw]
+            with dp_ctx():
+                y = fn(*args_, residual=res)
+                y.backward(dy)
+            s_out.wait_stream(comp)
+            with torch.cuda.stream(s_out):
+                for t in (y, x.grad, s2.grad):
+                    t.record_stream(s_out)
+                outs["y"][sl].copy_(y.detach(), non_blocking=True)
+                outs["dx"][sl].copy_(x.grad, non_blocking=True)
+                outs["d2"][sl].copy_(s2.grad, non_blocking=True)
+        s_out.wait_stream(comp)
+        with torch.cuda.stream(s_out):
+            outs["dsw"].copy_(sw.grad, non_blocking=True)
+            if U is not None:
+                outs["dU"].copy_(U.grad, non_blocking=True)
+        comp.wait_stream(s_out)
 
     for _ in range(3):
         step()
     torch.cuda.synchronize()
     n = max(3, min(args.steps, 10))
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    e0.record()
+    e0.record(comp)
     for _ in range(n):
         step()
-    e1.record()
+    e1.record(comp)
     torch.cuda.synchronize()
     ms = e0.elapsed_time(e1) / n
     t = torch.tensor([ms], device=dev, dtype=torch.float64)
@@ -653,7 +677,7 @@ def end_to_end(args, wl, a, a_sw, fn, dev, world, dp_ctx) -> dict:
     ms = float(t.item())
     ntok = wl["B"] * wl["T"] * world
     return {"value": ntok / (ms / 1e3) / 1e6, "unit": UNIT, "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
-            "ms_per_step": ms, "steps": n}
+            "ms_per_step": ms, "steps": n, "pipeline": f"{rows} batch rows per step, upload / compute / download streams"}
 
 
 def main():

@@ -87,11 +87,13 @@ class _LowrankDynamicConvolutionFn(torch.autograd.Function):
         )
         if reduce_first:
             allreduce_shared_grad(dU_f32, ctx.group)
-            dU = torch.empty_like(U)
-            _lib.check(lib.dynconv_cast_f32(_lib.ptr(dU_f32), _lib.ptr(dU), R * W * D, code, stream))
+            # one cast of the reduced accumulator; dU and dstatic_w are row views of it
+            # (the reference also returns slices of one buffer, lowrank.py:295-299)
+            g = torch.empty((Rk, W * D), device=x.device, dtype=x.dtype)
+            _lib.check(lib.dynconv_cast_f32(_lib.ptr(dU_f32), _lib.ptr(g), Rk * W * D, code, stream))
+            dU = g[:R]
             if has_static:
-                dsw = torch.empty((W, D), device=x.device, dtype=x.dtype)
-                _lib.check(lib.dynconv_cast_f32(_lib.ptr(dU_f32[R]), _lib.ptr(dsw), W * D, code, stream))
+                dsw = g[R].view(W, D)
         z_dt, U_dt, sw_dt = ctx.dtypes
         if dz.dtype != z_dt:
             dz = dz.to(z_dt)
