@@ -33,8 +33,22 @@ int cuda_status(cudaError_t e, const char* what) {
   return set_error(DYNCONV_ERR_CUDA, "%s: %s", what, cudaGetErrorString(e));
 }
 
+int ensure_context() {
+  thread_local int bound_device = -1;
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return cuda_status(e, "cudaGetDevice");
+  if (dev == bound_device) return DYNCONV_OK;
+  e = cudaSetDevice(dev);
+  if (e != cudaSuccess) return cuda_status(e, "cudaSetDevice");
+  bound_device = dev;
+  return DYNCONV_OK;
+}
+
 int encode_tensor_map_bf16(CUtensorMap* map, const void* base, int rank, const cuuint64_t* dims,
                            const cuuint64_t* strides_bytes, const cuuint32_t* box) {
+  int s = ensure_context();
+  if (s) return s;
   using EncodeFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
                                 const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
                                 CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);

@@ -28,6 +28,12 @@ int cuda_status(cudaError_t e, const char* what);
 // Number of SMs of the current device (cached per device).
 int sm_count();
 
+// Makes the current device's primary context current on the calling thread
+// (cudaSetDevice does so since CUDA 12), once per thread and device.  Driver-API
+// calls such as cuTensorMapEncodeTiled need a current context, and a thread that
+// has made no runtime call yet -- autograd's backward worker, say -- has none.
+int ensure_context();
+
 // Encodes a tiled, no-swizzle, zero-fill bf16 TMA descriptor (cuTensorMapEncodeTiled,
 // reached through the runtime's driver entry point).  `strides_bytes` has rank-1
 // entries (dimension 0 is dense).  DYNCONV_OK or DYNCONV_ERR_CUDA.

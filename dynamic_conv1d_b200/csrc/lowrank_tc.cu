@@ -71,6 +71,7 @@ EncodeTiledFn encode_fn() {
 int make_btd_map(CUtensorMap* map, const void* base, int64_t B, int64_t T, int64_t D, int box_d, int box_t) {
   EncodeTiledFn fn = encode_fn();
   if (!fn) return set_error(DYNCONV_ERR_CUDA, "cuTensorMapEncodeTiled unavailable");
+  if (int s = ensure_context()) return s;
   cuuint64_t dims[3] = {(cuuint64_t)D, (cuuint64_t)T, (cuuint64_t)B};
   cuuint64_t strides[2] = {(cuuint64_t)D * 2, (cuuint64_t)T * D * 2};
   cuuint32_t box[3] = {(cuuint32_t)box_d, (cuuint32_t)box_t, 1};
@@ -88,6 +89,7 @@ int make_btd_map(CUtensorMap* map, const void* base, int64_t B, int64_t T, int64
 int make_zpack_map(CUtensorMap* map, const void* base, int64_t B, int64_t T, int rkp, int rows) {
   EncodeTiledFn fn = encode_fn();
   if (!fn) return set_error(DYNCONV_ERR_CUDA, "cuTensorMapEncodeTiled unavailable");
+  if (int s = ensure_context()) return s;
   cuuint64_t dims[4] = {8, (cuuint64_t)T, (cuuint64_t)B, (cuuint64_t)(rkp / 8)};
   cuuint64_t strides[3] = {16, (cuuint64_t)T * 16, (cuuint64_t)B * T * 16};
   cuuint32_t box[4] = {8, (cuuint32_t)rows, 1, (cuuint32_t)(rkp / 8)};
@@ -101,30 +103,32 @@ int make_zpack_map(CUtensorMap* map, const void* base, int64_t B, int64_t T, int
 
 // z_pack[c][b][t][e] = z_ext[b, t, 8c + e]: z for ranks < R, 1.0 at rank R when the
 // static filter is fused (the reference's F.pad(z, (0, 1), value=1.0),
-// lowrank.py:224), 0 up to RKP.  One thread per (b, t).
+// lowrank.py:224), 0 up to RKP.  One thread per (8-rank chunk, token): consecutive
+// threads write consecutive 16-byte chunks.
 __global__ void __launch_bounds__(256) z_pack_kernel(const __nv_bfloat16* __restrict__ z,
                                                      __nv_bfloat16* __restrict__ zp, int64_t ntok, int R, int rkp,
                                                      int has_static) {
-  const int64_t tok = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
-  if (tok >= ntok) return;
+  const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= ntok * (rkp / 8)) return;
+  const int c = (int)(i / ntok);
+  const int64_t tok = i - (int64_t)c * ntok;
   const __nv_bfloat16* zr = z + tok * R;
-  for (int c = 0; c < rkp / 8; ++c) {
-    __align__(16) __nv_bfloat16 v[8];
+  __align__(16) __nv_bfloat16 v[8];
 #pragma unroll
-    for (int e = 0; e < 8; ++e) {
-      const int r = 8 * c + e;
-      v[e] = r < R ? zr[r] : __float2bfloat16_rn((r == R && has_static) ? 1.f : 0.f);
-    }
-    *reinterpret_cast<uint4*>(zp + ((size_t)c * ntok + tok) * 8) = *reinterpret_cast<const uint4*>(v);
+  for (int e = 0; e < 8; ++e) {
+    const int r = 8 * c + e;
+    v[e] = r < R ? zr[r] : __float2bfloat16_rn((r == R && has_static) ? 1.f : 0.f);
   }
+  *reinterpret_cast<uint4*>(zp + i * 8) = *reinterpret_cast<const uint4*>(v);
 }
 
 size_t zpack_bytes(int64_t B, int64_t T, int rkp) { return ((size_t)B * T * rkp * 2 + 255) / 256 * 256; }
 
 int z_pack_launch(const void* z, void* zp, int64_t B, int64_t T, int R, int rkp, bool has_static, cudaStream_t st) {
   const int64_t ntok = B * T;
-  z_pack_kernel<<<(unsigned)((ntok + 255) / 256), 256, 0, st>>>((const __nv_bfloat16*)z, (__nv_bfloat16*)zp, ntok, R,
-                                                               rkp, has_static ? 1 : 0);
+  const int64_t nthreads = ntok * (rkp / 8);
+  z_pack_kernel<<<(unsigned)((nthreads + 255) / 256), 256, 0, st>>>((const __nv_bfloat16*)z, (__nv_bfloat16*)zp,
+                                                                   ntok, R, rkp, has_static ? 1 : 0);
   DYNCONV_CHECK_LAUNCH("z_pack_kernel");
   return DYNCONV_OK;
 }

@@ -1,0 +1,129 @@
+"""The data-parallel backward path on a GPU, over a one-rank NCCL process group.
+
+Inside ``data_parallel()`` the backward of both ops takes the other branch: the
+kernels leave the float32 shared-gradient accumulator unconverted, it is
+all-reduced through torch.distributed (NCCL), and then cast to the parameter
+dtype (lowrank: one cast of the whole [R_kernel, W*D] buffer, returned as row
+views).  A SUM over one rank is the identity, so every gradient must equal the
+single-process path bit for bit.  Runs in a child process so the process group
+never leaks into other tests."""
+from __future__ import annotations
+
+import os
+import socket
+import subprocess
+import sys
+import textwrap
+
+import pytest
+
+pytestmark = pytest.mark.gpu
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+
+CHILD = textwrap.dedent(
+    """
+    import sys, datetime
+    import torch, torch.distributed as dist
+    sys.path.insert(0, {root!r})
+    from dynamic_conv1d_b200 import data_parallel, headwise_dynamic_convolution, lowrank_dynamic_convolution
+    dist.init_process_group("nccl", init_method="tcp://127.0.0.1:{port}", rank=0, world_size=1,
+                            timeout=datetime.timedelta(seconds=60), device_id=torch.device("cuda", 0))
+    dev = torch.device("cuda", 0)
+    g = torch.Generator().manual_seed(5)
+    bf = torch.bfloat16
+    def rnd(*s, scale=1.0):
+        return (torch.randn(*s, generator=g) * scale).to(bf).to(dev)
+
+    def grads(fn, cpu_leaves, dy, dp):
+        leaves = [t.clone().requires_grad_() for t in cpu_leaves]
+        if dp:
+            with data_parallel():
+                y = fn(*leaves, residual=True)
+                y.backward(dy)
+        else:
+            y = fn(*leaves, residual=True)
+            y.backward(dy)
+        torch.cuda.synchronize()
+        return [y.detach()] + [l.grad for l in leaves]
+
+    B, T, D, W = 2, 200, 256, 4
+    x, dy = rnd(B, T, D), rnd(B, T, D)
+    cases = {{
+        "lowrank_static": (lowrank_dynamic_convolution, [x, rnd(B, T, 15), rnd(15, W * D, scale=0.25), rnd(W, D, scale=0.3)]),
+        "lowrank_nostatic": (lowrank_dynamic_convolution, [x, rnd(B, T, 16), rnd(16, W * D, scale=0.25)]),
+        "headwise_hs32": (headwise_dynamic_convolution, [x, rnd(B, T, D // 32, W, scale=0.3), rnd(W, D, scale=0.3)]),
+    }}
+    for name, (fn, leaves) in cases.items():
+        ref = grads(fn, leaves, dy, dp=False)
+        got = grads(fn, leaves, dy, dp=True)
+        for i, (a, b) in enumerate(zip(ref, got)):
+            assert a.shape == b.shape and a.dtype == b.dtype, (name, i, a.shape, b.shape, a.dtype, b.dtype)
+            assert torch.equal(a, b), (name, i, (a.float() - b.float()).abs().max().item())
+        print("ok", name)
+    dist.destroy_process_group()
+    """
+)
+
+
+def _free_port() -> int:
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def test_data_parallel_backward_matches_single_process(cuda_device):
+    code = CHILD.format(root=ROOT, port=_free_port())
+    r = subprocess.run([sys.executable, "-c", code], capture_output=True, text=True, timeout=240)
+    assert r.returncode == 0, r.stdout[-2000:] + r.stderr[-4000:]
+    assert r.stdout.count("ok ") == 3, r.stdout
+
+
+THREAD_CHILD = textwrap.dedent(
+    """
+    import sys, threading
+    import torch
+    sys.path.insert(0, {root!r})
+    from dynamic_conv1d_b200 import _lib
+    lib = _lib.load()
+    dev = torch.device("cuda", 0)
+    g = torch.Generator().manual_seed(9)
+    B, T, D, R, W = 2, 130, 256, 15, 4
+    bf = torch.bfloat16
+    x = torch.randn(B, T, D, generator=g).to(bf).to(dev)
+    z = torch.randn(B, T, R, generator=g).to(bf).to(dev)
+    U = (torch.randn(R, W * D, generator=g) * 0.25).to(bf).to(dev)
+    sw = (torch.randn(W, D, generator=g) * 0.3).to(bf).to(dev)
+    nb = lib.dynconv_lr_fwd_workspace_bytes(B, T, D, R, W, 0, 1)
+    ws = torch.empty(nb, dtype=torch.uint8, device=dev)
+    torch.cuda.synchronize()
+
+    def call(y):
+        # a thread that has made no CUDA runtime call of its own
+        st = _lib.stream_of(x)
+        status[0] = lib.dynconv_lr_fwd(_lib.ptr(x), _lib.ptr(z), _lib.ptr(U), _lib.ptr(sw), _lib.ptr(y), _lib.ptr(ws),
+                                       nb, B, T, D, R, W, 0, 1, st)
+        if status[0] != 0:
+            status.append(lib.dynconv_last_error().decode())
+
+    y_thread, y_main = torch.empty_like(x), torch.empty_like(x)
+    status = [None]
+    th = threading.Thread(target=call, args=(y_thread,))
+    th.start(); th.join()
+    assert status[0] == 0, status
+    call(y_main)
+    assert status[0] == 0, status
+    torch.cuda.synchronize()
+    assert torch.equal(y_thread, y_main)
+    print("ok thread")
+    """
+)
+
+
+def test_entry_point_from_a_fresh_thread(cuda_device):
+    """TMA descriptor encoding is a driver call that needs a current context; the
+    library binds the device's primary context itself on a thread that has none."""
+    r = subprocess.run([sys.executable, "-c", THREAD_CHILD.format(root=ROOT)], capture_output=True, text=True,
+                       timeout=240)
+    assert r.returncode == 0, r.stdout[-2000:] + r.stderr[-4000:]
+    assert "ok thread" in r.stdout, r.stdout
