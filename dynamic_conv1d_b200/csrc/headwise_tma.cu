@@ -190,60 +190,51 @@ __device__ __forceinline__ float2 mul2(float2 a, float2 b) {
 }
 
 // dweight of one head and row: v[w] holds this lane's partial over its channels;
-// the 2^lg lanes of the head (consecutive, aligned) sum them and write the W taps
+// the 2^LG lanes of the head (consecutive, aligned) sum them and write the W taps
 // to dst (row_ok: this lane's row and channels are inside the tensor).  For W = 4
 // and W = 2 the first levels are a reduce-scatter (each lane keeps half of the
 // taps and sends the other half), so a head of 8 lanes costs 4 shuffles instead
-// of 12; every lane writes the taps it ends up owning.
-template <int W>
-__device__ __forceinline__ void head_reduce_store(float (&v)[W], int lane, int lg, bool row_ok, __nv_bfloat16* dst) {
+// of 12; every lane writes the taps it ends up owning.  LG is a compile-time
+// constant, so the whole butterfly is straight-line code.
+template <int W, int LG>
+__device__ __forceinline__ void head_reduce_store(float (&v)[W], int lane, bool row_ok, __nv_bfloat16* dst) {
   constexpr unsigned kAll = 0xffffffffu;
-  if constexpr (W == 4) {
-    if (lg == 0) {
-      if (row_ok) {
-        __align__(8) __nv_bfloat16 o[4];
-#pragma unroll
-        for (int w = 0; w < 4; ++w) o[w] = __float2bfloat16_rn(v[w]);
-        *reinterpret_cast<uint2*>(dst) = *reinterpret_cast<const uint2*>(o);
-      }
-      return;
-    }
+  constexpr int G = 1 << LG;  // lanes per head
+  if constexpr (W == 4 && LG >= 1) {
     // level 1 (lanes l, l^1): the odd lane keeps taps 2,3, the even lane taps 0,1
     const bool up1 = lane & 1;
     float k0 = up1 ? v[2] : v[0], k1 = up1 ? v[3] : v[1];
     const float s0 = up1 ? v[0] : v[2], s1 = up1 ? v[1] : v[3];
     k0 += __shfl_xor_sync(kAll, s0, 1);
     k1 += __shfl_xor_sync(kAll, s1, 1);
-    if (lg == 1) {
-      if (row_ok) {
-        __nv_bfloat162 o = __floats2bfloat162_rn(k0, k1);
-        *reinterpret_cast<__nv_bfloat162*>(dst + (up1 ? 2 : 0)) = o;
-      }
-      return;
+    if constexpr (LG == 1) {
+      if (row_ok) *reinterpret_cast<__nv_bfloat162*>(dst + (up1 ? 2 : 0)) = __floats2bfloat162_rn(k0, k1);
+    } else {
+      // level 2 (lanes l, l^2): keep one tap
+      const bool up2 = lane & 2;
+      float k = up2 ? k1 : k0;
+      k += __shfl_xor_sync(kAll, up2 ? k0 : k1, 2);
+#pragma unroll
+      for (int o = 4; o < G; o <<= 1) k += __shfl_xor_sync(kAll, k, o);
+      if (row_ok && (lane & (G - 1)) < 4) dst[(up1 ? 2 : 0) + (up2 ? 1 : 0)] = __float2bfloat16_rn(k);
     }
-    // level 2 (lanes l, l^2): keep one tap
-    const bool up2 = lane & 2;
-    float k = up2 ? k1 : k0;
-    k += __shfl_xor_sync(kAll, up2 ? k0 : k1, 2);
-    for (int o = 4; o < (1 << lg); o <<= 1) k += __shfl_xor_sync(kAll, k, o);
-    if (row_ok && (lane & ((1 << lg) - 1)) < 4) dst[(up1 ? 2 : 0) + (up2 ? 1 : 0)] = __float2bfloat16_rn(k);
-  } else if constexpr (W == 2) {
-    if (lg == 0) {
-      if (row_ok) *reinterpret_cast<__nv_bfloat162*>(dst) = __floats2bfloat162_rn(v[0], v[1]);
-      return;
-    }
+  } else if constexpr (W == 2 && LG >= 1) {
     const bool up1 = lane & 1;
     float k = up1 ? v[1] : v[0];
     k += __shfl_xor_sync(kAll, up1 ? v[0] : v[1], 1);
-    for (int o = 2; o < (1 << lg); o <<= 1) k += __shfl_xor_sync(kAll, k, o);
-    if (row_ok && (lane & ((1 << lg) - 1)) < 2) dst[up1 ? 1 : 0] = __float2bfloat16_rn(k);
+#pragma unroll
+    for (int o = 2; o < G; o <<= 1) k += __shfl_xor_sync(kAll, k, o);
+    if (row_ok && (lane & (G - 1)) < 2) dst[up1 ? 1 : 0] = __float2bfloat16_rn(k);
   } else {
-    for (int o = 1; o < (1 << lg); o <<= 1)
+#pragma unroll
+    for (int o = 1; o < G; o <<= 1)
 #pragma unroll
       for (int w = 0; w < W; ++w) v[w] += __shfl_xor_sync(kAll, v[w], o);
-    if (row_ok && (lane & ((1 << lg) - 1)) == 0) {
+    if (row_ok && (lane & (G - 1)) == 0) {
+      __align__(8) __nv_bfloat16 o[W];
 #pragma unroll
-      for (int w = 0; w < W; ++w) dst[w] = __float2bfloat16_rn(v[w]);
+      for (int w = 0; w < W; ++w) o[w] = __float2bfloat16_rn(v[w]);
+      st_bf16<W, pow2_align(2 * W)>(dst, o);
     }
   }
 }
@@ -273,7 +264,7 @@ __device__ __forceinline__ void load_row_weights(const __nv_bfloat16* wrow, int 
     for (int w = 0; w < W; ++w) wt[j][w] = __bfloat162float(v[j * W + w]);
 }
 
-template <int K, int W, bool BWD, bool SPLIT>
+template <int K, int W, bool BWD, bool SPLIT, int LG>
 __global__ void __launch_bounds__(kHwThreads, kCtasPerSm)
     hw_tma_kernel(const __grid_constant__ CUtensorMap xmap, const __grid_constant__ CUtensorMap dymap,
                   const __grid_constant__ CUtensorMap wmap, const __nv_bfloat16* __restrict__ sw,
@@ -444,7 +435,7 @@ __global__ void __launch_bounds__(kHwThreads, kCtasPerSm)
             for (int q = 1; q < P; ++q) a = fma2(dyf[rr][q], xf[rr + W - 1 - w][q], a);
             hsum[w] = a.x + a.y;
           }
-          head_reduce_store<W>(hsum, lane, log2hs - 2, row_ok,
+          head_reduce_store<W, LG>(hsum, lane, row_ok,
                                dw + (((size_t)b * T + t) * H + (dch >> log2hs)) * W);
         } else {
           // HPT heads per lane, K channels each (K = 1 or 2)
@@ -524,7 +515,7 @@ HwSplit hw_split(int64_t B, int64_t T, int64_t D, int TR) {
 
 int hw_tr(int K, bool bwd) { return bwd ? 16 : (K == kVec ? 64 : 16); }
 
-template <int K, int W, bool BWD, bool SPLIT>
+template <int K, int W, bool BWD, bool SPLIT, int LG>
 int launch_hw_tma(const void* x, const void* wgt, const void* sw, const void* dy, void* out, void* dw, float* part,
                   int64_t B, int64_t T, int64_t D, int64_t H, int log2hs, int residual, cudaStream_t st) {
   using G = HwGeo<K, W, BWD>;
@@ -560,7 +551,7 @@ int launch_hw_tma(const void* x, const void* wgt, const void* sw, const void* dy
     const cuuint32_t box[4] = {128, (cuuint32_t)wchunks, (cuuint32_t)G::ROWS_A, 1};
     if ((s = encode_tensor_map_bf16(&wmap, wgt, 4, dims, strides, box))) return s;
   }
-  auto kern = hw_tma_kernel<K, W, BWD, SPLIT>;
+  auto kern = hw_tma_kernel<K, W, BWD, SPLIT, LG>;
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, G::SMEM);
   if (e != cudaSuccess) {
     cudaGetLastError();
@@ -574,6 +565,22 @@ int launch_hw_tma(const void* x, const void* wgt, const void* sw, const void* dy
   return DYNCONV_OK;
 }
 
+// Backward with head_size >= kVec: lanes per head 2^LG = head_size / kVec as a
+// compile-time constant (head_size 4..128).
+template <int W, bool BWD>
+int launch_hw_tma_lg(const void* x, const void* wgt, const void* sw, const void* dy, void* out, void* dw, float* part,
+                     int64_t B, int64_t T, int64_t D, int64_t H, int log2hs, int residual, cudaStream_t st) {
+  switch (log2hs - 2) {
+    case 0: return launch_hw_tma<kVec, W, BWD, false, 0>(x, wgt, sw, dy, out, dw, part, B, T, D, H, log2hs, residual, st);
+    case 1: return launch_hw_tma<kVec, W, BWD, false, 1>(x, wgt, sw, dy, out, dw, part, B, T, D, H, log2hs, residual, st);
+    case 2: return launch_hw_tma<kVec, W, BWD, false, 2>(x, wgt, sw, dy, out, dw, part, B, T, D, H, log2hs, residual, st);
+    case 3: return launch_hw_tma<kVec, W, BWD, false, 3>(x, wgt, sw, dy, out, dw, part, B, T, D, H, log2hs, residual, st);
+    case 4: return launch_hw_tma<kVec, W, BWD, false, 4>(x, wgt, sw, dy, out, dw, part, B, T, D, H, log2hs, residual, st);
+    case 5: return launch_hw_tma<kVec, W, BWD, false, 5>(x, wgt, sw, dy, out, dw, part, B, T, D, H, log2hs, residual, st);
+    default: return set_error(DYNCONV_ERR_UNSUPPORTED, "headwise TMA path: head_size %d", 1 << log2hs);
+  }
+}
+
 template <bool BWD>
 int hw_tma_dispatch(const void* x, const void* wgt, const void* sw, const void* dy, void* out, void* dw, float* part,
                     int64_t B, int64_t T, int64_t D, int64_t H, int W, int log2hs, int residual, cudaStream_t st) {
@@ -581,8 +588,10 @@ int hw_tma_dispatch(const void* x, const void* wgt, const void* sw, const void* 
 #define DYNCONV_HWT(KK, WW)                                                                                       \
   if (K == KK && W == WW) {                                                                                       \
     if (KK == 1 && D % kCB == 0)                                                                                  \
-      return launch_hw_tma<KK, WW, BWD, KK == 1>(x, wgt, sw, dy, out, dw, part, B, T, D, H, log2hs, residual, st); \
-    return launch_hw_tma<KK, WW, BWD, false>(x, wgt, sw, dy, out, dw, part, B, T, D, H, log2hs, residual, st);     \
+      return launch_hw_tma<KK, WW, BWD, KK == 1, 0>(x, wgt, sw, dy, out, dw, part, B, T, D, H, log2hs, residual, st); \
+    if (KK == kVec && BWD) return launch_hw_tma_lg<WW, BWD>(x, wgt, sw, dy, out, dw, part, B, T, D, H, log2hs,     \
+                                                             residual, st);                                        \
+    return launch_hw_tma<KK, WW, BWD, false, 0>(x, wgt, sw, dy, out, dw, part, B, T, D, H, log2hs, residual, st);  \
   }
   DYNCONV_HWT(1, 1) DYNCONV_HWT(1, 2) DYNCONV_HWT(1, 3) DYNCONV_HWT(1, 4)
   DYNCONV_HWT(2, 1) DYNCONV_HWT(2, 2) DYNCONV_HWT(2, 3) DYNCONV_HWT(2, 4)
