@@ -7,11 +7,14 @@ hand-written sm_100a CUDA kernels (see ``include/dynconv.h``).
 """
 from .headwise import headwise_dynamic_convolution
 from .lowrank import lowrank_dynamic_convolution
+from .modules import LowRankDynamicShortConvolution, QKVLowRankDynamicShortConvolution
 from .parallel import data_parallel, shard_rows
 
 __all__ = [
     "headwise_dynamic_convolution",
     "lowrank_dynamic_convolution",
+    "LowRankDynamicShortConvolution",
+    "QKVLowRankDynamicShortConvolution",
     "data_parallel",
     "shard_rows",
 ]
