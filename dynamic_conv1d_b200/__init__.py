@@ -9,6 +9,7 @@ from .headwise import headwise_dynamic_convolution
 from .lowrank import lowrank_dynamic_convolution
 from .modules import LowRankDynamicShortConvolution, QKVLowRankDynamicShortConvolution
 from .parallel import data_parallel, shard_rows
+from .sequence_parallel import headwise_dynamic_convolution_sp, lowrank_dynamic_convolution_sp
 
 __all__ = [
     "headwise_dynamic_convolution",
@@ -16,5 +17,7 @@ __all__ = [
     "LowRankDynamicShortConvolution",
     "QKVLowRankDynamicShortConvolution",
     "data_parallel",
+    "lowrank_dynamic_convolution_sp",
+    "headwise_dynamic_convolution_sp",
     "shard_rows",
 ]

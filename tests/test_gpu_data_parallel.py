@@ -127,3 +127,54 @@ def test_entry_point_from_a_fresh_thread(cuda_device):
                        timeout=240)
     assert r.returncode == 0, r.stdout[-2000:] + r.stderr[-4000:]
     assert "ok thread" in r.stdout, r.stdout
+
+
+SP_CHILD = textwrap.dedent(
+    """
+    import sys, datetime
+    import torch, torch.distributed as dist
+    sys.path.insert(0, {root!r})
+    from dynamic_conv1d_b200 import (headwise_dynamic_convolution, headwise_dynamic_convolution_sp,
+                                     lowrank_dynamic_convolution, lowrank_dynamic_convolution_sp)
+    dist.init_process_group("nccl", init_method="tcp://127.0.0.1:{port}", rank=0, world_size=1,
+                            timeout=datetime.timedelta(seconds=60), device_id=torch.device("cuda", 0))
+    dev = torch.device("cuda", 0)
+    g = torch.Generator().manual_seed(6)
+    bf = torch.bfloat16
+    def rnd(*s, scale=1.0):
+        return (torch.randn(*s, generator=g) * scale).to(bf).to(dev)
+    def rel(a, b):
+        return ((a.float() - b.float()).norm() / b.float().norm().clamp_min(1e-30)).item()
+    B, T, D, W = 2, 200, 256, 4
+    x, dy = rnd(B, T, D), rnd(B, T, D)
+    cases = {{
+        "lowrank": (lowrank_dynamic_convolution, lowrank_dynamic_convolution_sp,
+                    [x, rnd(B, T, 15), rnd(15, W * D, scale=0.25), rnd(W, D, scale=0.3)]),
+        "headwise": (headwise_dynamic_convolution, headwise_dynamic_convolution_sp,
+                     [x, rnd(B, T, D // 32, W, scale=0.3), rnd(W, D, scale=0.3)]),
+    }}
+    for name, (fn, fn_sp, leaves0) in cases.items():
+        outs = []
+        for f in (fn, fn_sp):
+            leaves = [t.clone().requires_grad_() for t in leaves0]
+            y = f(*leaves, residual=True)
+            y.backward(dy)
+            torch.cuda.synchronize()
+            outs.append([y.detach()] + [l.grad for l in leaves])
+        for i, (a, b) in enumerate(zip(*outs)):
+            assert a.shape == b.shape, (name, i)
+            e = rel(b, a)
+            assert e <= (1e-2 if i == 0 else 2e-2), (name, i, e)
+        print("ok", name)
+    dist.destroy_process_group()
+    """
+)
+
+
+def test_sequence_parallel_one_rank_matches_direct(cuda_device):
+    """Time-sharded wrappers on one NCCL rank: the halo is the zero padding and the
+    results match the direct op within the bf16 tolerances."""
+    code = SP_CHILD.format(root=ROOT, port=_free_port())
+    r = subprocess.run([sys.executable, "-c", code], capture_output=True, text=True, timeout=240)
+    assert r.returncode == 0, r.stdout[-2000:] + r.stderr[-4000:]
+    assert r.stdout.count("ok ") == 2, r.stdout

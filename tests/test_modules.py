@@ -66,4 +66,4 @@ def test_qkv_module_matches_separate_modules(cuda_device):
     outs = qkv(q, k, v, pre)
     for mm, t, o in zip((qkv.q, qkv.k, qkv.v), (q, k, v), outs):
         ref = mm(t, pre)
-        assert rel_l2(o.float().cpu().numpy(), ref.float().cpu().numpy()) <= 1e-2
+        assert rel_l2(o.detach().float().cpu().numpy(), ref.detach().float().cpu().numpy()) <= 1e-2
