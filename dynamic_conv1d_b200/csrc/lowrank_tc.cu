@@ -742,7 +742,6 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
       const int s = k % kBwdStages, p = k % NP;
       const int tile = j0 + k, b = tile / sp.tiles_row, t0 = (tile % sp.tiles_row) * kBT;
       if (!dead) dead = !mbar_wait(&full_bar[s], (k / kBwdStages) & 1, kErrWaitEpilogue, &abort_flag);
-      if (!dead) dead = !mbar_wait(&pe_bar[p], ((k / NP) & 1) ^ 1, kErrWaitEpilogue, &abort_flag);
       const __nv_bfloat16* dys = reinterpret_cast<const __nv_bfloat16*>(smem + L::kOffDy + s * L::kTileStride);
       const __nv_bfloat16* xs = reinterpret_cast<const __nv_bfloat16*>(smem + L::kOffX + s * L::kTileStride);
       uint8_t* pbuf = smem + L::kOffP + p * W * L::kPTap;
@@ -773,6 +772,9 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
           }
           // P^T in TMEM is single-buffered: wait for the MMA-2 of the previous tile
           if (L::kPT && h == 0) dead = !mbar_wait(&pte_bar, (k & 1) ^ 1, kErrWaitEpilogue, &abort_flag);
+          // the P buffer is needed from the first P store on (with one buffer, the
+          // previous tile's MMA-2/3 overlap this tile's first dx half)
+          if (!dead && h == 0) dead = !mbar_wait(&pe_bar[p], ((k / NP) & 1) ^ 1, kErrWaitEpilogue, &abort_flag);
           if (!dead) {
 #pragma unroll
             for (int w = 0; w < W; ++w) {
