@@ -32,6 +32,16 @@ def ref_lowrank(x, z, U, static_w, residual=False):
     return y + x if residual else y
 
 
+def ref_headwise(x, weight, static_w, residual=False):
+    B, T, D = x.shape
+    H, W = weight.shape[2], weight.shape[3]
+    w = weight.repeat_interleave(D // H, dim=2)  # [B, T, D, W]
+    if static_w is not None:
+        w = w + static_w.t()
+    y = sum(w[..., k] * F.pad(x, (0, 0, k, 0))[:, :T] for k in range(W))
+    return y + x if residual else y
+
+
 def _inputs(B=2, T=24, D=8, R=3, W=4, seed=0):
     g = torch.Generator().manual_seed(seed)
     return (torch.randn(B, T, D, generator=g), torch.randn(B, T, R, generator=g),
@@ -39,25 +49,38 @@ def _inputs(B=2, T=24, D=8, R=3, W=4, seed=0):
             torch.randn(B, T, D, generator=g))
 
 
-def _worker(rank, world, port, W, q):
+def _hw_inputs(B=2, T=24, D=8, H=4, W=4, seed=0):
+    g = torch.Generator().manual_seed(seed)
+    return (torch.randn(B, T, D, generator=g), torch.randn(B, T, H, W, generator=g) * 0.5,
+            torch.randn(W, D, generator=g) * 0.5, torch.randn(B, T, D, generator=g))
+
+
+def _worker(rank, world, port, W, q, kind="lowrank"):
     try:
         from dynamic_conv1d_b200.sequence_parallel import sequence_parallel
 
         os.environ["MASTER_ADDR"] = "127.0.0.1"
         os.environ["MASTER_PORT"] = str(port)
         dist.init_process_group("gloo", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=60))
-        x, z, U, sw, dy = _inputs(W=W)
+        if kind == "lowrank":
+            x, z, U, sw, dy = _inputs(W=W)
+            shared = [U, sw]
+            fn = ref_lowrank
+        else:
+            x, z, sw, dy = _hw_inputs(W=W)
+            shared = [sw]
+            fn = ref_headwise
         T = x.shape[1]
         lo, hi = rank * T // world, (rank + 1) * T // world
         xl = x[:, lo:hi].clone().requires_grad_()
         zl = z[:, lo:hi].clone().requires_grad_()
-        Ul, swl = U.clone().requires_grad_(), sw.clone().requires_grad_()
-        y = sequence_parallel(ref_lowrank, xl, zl, Ul, swl, residual=True, W=W)
+        sh = [p.clone().requires_grad_() for p in shared]
+        y = sequence_parallel(fn, xl, zl, *sh, residual=True, W=W)
         y.backward(dy[:, lo:hi])
         # the torch stand-in does not all-reduce its shared gradients; do it here
-        for p in (Ul, swl):
+        for p in sh:
             dist.all_reduce(p.grad)
-        q.put((rank, lo, hi, y.detach(), xl.grad, zl.grad, Ul.grad, swl.grad))
+        q.put((rank, lo, hi, y.detach(), xl.grad, zl.grad) + tuple(p.grad for p in sh))
         dist.barrier()
         dist.destroy_process_group()
     except Exception as e:  # report instead of hanging the parent
@@ -85,9 +108,35 @@ def test_sequence_parallel_matches_full_sequence(world, W):
     leaves = [t.clone().requires_grad_() for t in (x, z, U, sw)]
     y = ref_lowrank(*leaves, residual=True)
     y.backward(dy)
-    for rank, lo, hi, yl, gx, gz, gU, gsw in res:
+    _check(res, leaves, y)
+
+
+def _check(res, leaves, y):
+    for rank, lo, hi, yl, gx, gz, *gshared in res:
         torch.testing.assert_close(yl, y.detach()[:, lo:hi], rtol=1e-5, atol=1e-5)
         torch.testing.assert_close(gx, leaves[0].grad[:, lo:hi], rtol=1e-5, atol=1e-5)
         torch.testing.assert_close(gz, leaves[1].grad[:, lo:hi], rtol=1e-5, atol=1e-5)
-        torch.testing.assert_close(gU, leaves[2].grad, rtol=1e-4, atol=1e-4)
-        torch.testing.assert_close(gsw, leaves[3].grad, rtol=1e-4, atol=1e-4)
+        for g, leaf in zip(gshared, leaves[2:]):
+            torch.testing.assert_close(g, leaf.grad, rtol=1e-4, atol=1e-4)
+
+
+def test_sequence_parallel_headwise_matches_full_sequence():
+    world, W = 3, 4
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        port = s.getsockname()[1]
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    procs = [ctx.Process(target=_worker, args=(r, world, port, W, q, "headwise")) for r in range(world)]
+    for p in procs:
+        p.start()
+    res = [q.get(timeout=180) for _ in range(world)]
+    for p in procs:
+        p.join(timeout=60)
+    for r in res:
+        assert r[1] != "error", r[2]
+    x, w, sw, dy = _hw_inputs(W=W)
+    leaves = [t.clone().requires_grad_() for t in (x, w, sw)]
+    y = ref_headwise(*leaves, residual=True)
+    y.backward(dy)
+    _check(res, leaves, y)
