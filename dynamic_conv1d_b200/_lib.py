@@ -7,6 +7,7 @@ cannot be loaded, every op raises.
 from __future__ import annotations
 
 import ctypes
+import functools
 import os
 import threading
 
@@ -92,6 +93,18 @@ def dtype_code(dtype: torch.dtype) -> int:
         return _TORCH_DTYPES[dtype]
     except KeyError:
         raise TypeError(f"dynamic convolution supports bfloat16 and float32 tensors, got {dtype}") from None
+
+
+def on_device(fn):
+    """Runs an autograd forward/backward with its first tensor's device current:
+    the library launches on the current device, the stream comes from the tensor."""
+
+    @functools.wraps(fn)
+    def wrapper(ctx, first, *args):
+        with torch.cuda.device(first.device):
+            return fn(ctx, first, *args)
+
+    return wrapper
 
 
 def ptr(t: torch.Tensor | None):

@@ -18,6 +18,7 @@ class _HeadwiseDynamicConvolutionFn(torch.autograd.Function):
     """Mirrors ``_HeadwiseDynamicConvolutionFn`` (headwise.py:218-309)."""
 
     @staticmethod
+    @_lib.on_device
     def forward(ctx, x, weight, static_w, residual):
         B, T, D = x.shape
         H = weight.shape[2]
@@ -43,6 +44,7 @@ class _HeadwiseDynamicConvolutionFn(torch.autograd.Function):
         return y
 
     @staticmethod
+    @_lib.on_device
     def backward(ctx, dy):
         dy = dy.contiguous()
         x, w_k, static_w = ctx.saved_tensors

@@ -28,6 +28,7 @@ class _LowrankDynamicConvolutionFn(torch.autograd.Function):
     """Mirrors ``_LowrankDynamicConvolutionFn`` (lowrank.py:214-299)."""
 
     @staticmethod
+    @_lib.on_device
     def forward(ctx, x, z, U, static_w, residual):
         B, T, D = x.shape
         R = z.shape[-1]
@@ -56,6 +57,7 @@ class _LowrankDynamicConvolutionFn(torch.autograd.Function):
         return y
 
     @staticmethod
+    @_lib.on_device
     def backward(ctx, dy):
         dy = dy.contiguous()
         x, z, U, static_w = ctx.saved_tensors

@@ -178,3 +178,43 @@ def test_sequence_parallel_one_rank_matches_direct(cuda_device):
     r = subprocess.run([sys.executable, "-c", code], capture_output=True, text=True, timeout=240)
     assert r.returncode == 0, r.stdout[-2000:] + r.stderr[-4000:]
     assert r.stdout.count("ok ") == 2, r.stdout
+
+
+def test_tensors_on_a_non_current_device():
+    """Tensors on cuda:1 while cuda:0 is current: the Functions make the tensors'
+    device current around their library calls (needs two GPUs)."""
+    import torch
+
+    from dynamic_conv1d_b200 import headwise_dynamic_convolution, lowrank_dynamic_convolution
+
+    if not torch.cuda.is_available() or torch.cuda.device_count() < 2:
+        pytest.skip("needs two CUDA devices")
+    dev = torch.device("cuda", 1)
+    g = torch.Generator().manual_seed(8)
+    bf = torch.bfloat16
+
+    def rnd(*s, scale=1.0):
+        return (torch.randn(*s, generator=g) * scale).to(bf)
+
+    B, T, D, W = 2, 150, 256, 4
+    cpu = {"x": rnd(B, T, D), "dy": rnd(B, T, D), "z": rnd(B, T, 15), "U": rnd(15, W * D, scale=0.25),
+           "sw": rnd(W, D, scale=0.3), "w": rnd(B, T, D // 32, W, scale=0.3)}
+
+    def run(current):
+        torch.cuda.set_device(current)
+        t = {k: v.to(dev) for k, v in cpu.items()}
+        outs = []
+        for fn, args in ((lowrank_dynamic_convolution, ["x", "z", "U", "sw"]),
+                         (headwise_dynamic_convolution, ["x", "w", "sw"])):
+            leaves = [t[a].clone().requires_grad_() for a in args]
+            y = fn(*leaves, residual=True)
+            y.backward(t["dy"])
+            torch.cuda.synchronize(dev)
+            outs += [y.detach()] + [l.grad for l in leaves]
+        return outs
+
+    other = run(0)
+    same = run(1)
+    torch.cuda.set_device(0)
+    for a, b in zip(other, same):
+        assert a.device == dev and torch.equal(a, b)
