@@ -218,3 +218,69 @@ def test_tensors_on_a_non_current_device():
     torch.cuda.set_device(0)
     for a, b in zip(other, same):
         assert a.device == dev and torch.equal(a, b)
+
+
+SP2_SCRIPT = textwrap.dedent(
+    """
+    import datetime, os, sys
+    import torch, torch.distributed as dist
+    sys.path.insert(0, {root!r})
+    from dynamic_conv1d_b200 import (headwise_dynamic_convolution, headwise_dynamic_convolution_sp,
+                                     lowrank_dynamic_convolution, lowrank_dynamic_convolution_sp)
+    rank, world = int(os.environ["RANK"]), int(os.environ["WORLD_SIZE"])
+    dev = torch.device("cuda", rank)
+    torch.cuda.set_device(dev)
+    dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=60), device_id=dev)
+    g = torch.Generator().manual_seed(12)
+    bf = torch.bfloat16
+    def rnd(*s, scale=1.0):
+        return (torch.randn(*s, generator=g) * scale).to(bf)
+    def rel(a, b):
+        return ((a.float() - b.float()).norm() / b.float().norm().clamp_min(1e-30)).item()
+    B, T, D, W = 2, 256, 256, 4
+    x, dy = rnd(B, T, D), rnd(B, T, D)
+    cases = {{
+        "lowrank": (lowrank_dynamic_convolution, lowrank_dynamic_convolution_sp,
+                    [x, rnd(B, T, 15), rnd(15, W * D, scale=0.25), rnd(W, D, scale=0.3)], 2),
+        "headwise": (headwise_dynamic_convolution, headwise_dynamic_convolution_sp,
+                     [x, rnd(B, T, D // 32, W, scale=0.3), rnd(W, D, scale=0.3)], 2),
+    }}
+    lo, hi = rank * T // world, (rank + 1) * T // world
+    for name, (fn, fn_sp, cpu, n_local) in cases.items():
+        # time-sharded: x and the mixing input are split, the shared parameters replicated
+        leaves = [t[:, lo:hi].contiguous().to(dev) if i < n_local else t.to(dev) for i, t in enumerate(cpu)]
+        leaves = [t.requires_grad_() for t in leaves]
+        y = fn_sp(*leaves, residual=True)
+        y.backward(dy[:, lo:hi].contiguous().to(dev))
+        torch.cuda.synchronize()
+        # full sequence on this GPU
+        full = [t.to(dev).requires_grad_() for t in cpu]
+        yf = fn(*full, residual=True)
+        yf.backward(dy.to(dev))
+        torch.cuda.synchronize()
+        pairs = [(y, yf[:, lo:hi])] + [(l.grad, f.grad[:, lo:hi]) for l, f in zip(leaves[:n_local], full[:n_local])] \\
+            + [(l.grad, f.grad) for l, f in zip(leaves[n_local:], full[n_local:])]
+        for i, (a, b) in enumerate(pairs):
+            e = rel(a, b)
+            assert e <= (1e-2 if i == 0 else 2e-2), (name, rank, i, e)
+        print("ok", name, rank, flush=True)
+    dist.barrier()
+    dist.destroy_process_group()
+    """
+)
+
+
+def test_sequence_parallel_two_gpus(tmp_path):
+    """Time axis split over two GPUs (NCCL point-to-point halo exchange): each rank's
+    output and gradients match the full-sequence computation (needs two GPUs)."""
+    import torch
+
+    if not torch.cuda.is_available() or torch.cuda.device_count() < 2:
+        pytest.skip("needs two CUDA devices")
+    script = tmp_path / "sp2.py"
+    script.write_text(SP2_SCRIPT.format(root=ROOT))
+    r = subprocess.run([sys.executable, "-m", "torch.distributed.run", "--nnodes=1", "--nproc-per-node", "2",
+                        "--master-addr", "127.0.0.1", "--master-port", str(_free_port()), str(script)],
+                       capture_output=True, text=True, timeout=300)
+    assert r.returncode == 0, r.stdout[-2000:] + r.stderr[-4000:]
+    assert r.stdout.count("ok ") == 4, r.stdout
