@@ -855,8 +855,8 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
       const int tile = j0 + (int)(st / kBT), tok = (int)(st % kBT);
       const int b = tile / sp.tiles_row, t = (tile % sp.tiles_row) * kBT + tok;
       float4 a4 = make_float4(0.f, 0.f, 0.f, 0.f);
-#pragma unroll 4
-      for (int k2 = 0; k2 < sp.n_dblk; ++k2) {
+#pragma unroll 16
+      for (int k2 = 0; k2 < sp.n_dblk; ++k2) {  // all partial loads in flight, summed in order
         const float4 f =
             __ldcg(reinterpret_cast<const float4*>(dzp + (((size_t)k2 * sp.n_tiles + tile) * kBT + tok) * RKP) + rq);
         a4.x += f.x;
@@ -903,6 +903,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
     const int64_t lo = n4 * blockIdx.x / gridDim.x, hi = n4 * (blockIdx.x + 1) / gridDim.x;
     for (int64_t i = lo + threadIdx.x; i < hi; i += blockDim.x) {
       float4 a4 = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll 8
       for (int gg = 0; gg < sp.n_groups; ++gg) {
         const float4 f = __ldcg(reinterpret_cast<const float4*>(dUp) + (size_t)gg * n4 + i);
         a4.x += f.x;
