@@ -102,10 +102,22 @@ def make_inputs_np(wl: dict, rows: int | None = None, T: int | None = None, seed
 
 # ----------------------------------------------------------------- CPU leg
 
+def usable_cores() -> int:
+    """Host cores this process may run on (the affinity mask), at least 1."""
+    try:
+        return max(1, len(os.sched_getaffinity(0)))
+    except (AttributeError, OSError):
+        return max(1, os.cpu_count() or 1)
+
+
 def cpu_oracle_step(wl: dict, a: dict, threads: int):
-    """fwd+bwd of the oracle on the sample `a`, batch rows spread over threads."""
+    """fwd+bwd of the oracle on the sample `a`, one batch row per task, `threads`
+    workers.  numpy releases the GIL inside its array kernels and BLAS is held to
+    one thread per worker, so the rows run in parallel on `threads` cores."""
     import oracle  # test infrastructure; only the cpu_baseline / reference legs use it
     from concurrent.futures import ThreadPoolExecutor
+
+    from threadpoolctl import threadpool_limits
 
     B = a["x"].shape[0]
     res = bool(wl["residual"])
@@ -120,7 +132,7 @@ def cpu_oracle_step(wl: dict, a: dict, threads: int):
             g = oracle.headwise_bwd(a["x"][sl], a["weight"][sl], a["static_w"], a["dy"][sl], res)
         return y, g
 
-    with ThreadPoolExecutor(max_workers=threads) as ex:
+    with threadpool_limits(limits=1), ThreadPoolExecutor(max_workers=threads) as ex:
         outs = list(ex.map(one, range(B)))
     # shared gradients are summed over rows, as the full-batch reference does
     acc = outs[0][1][2].copy()
@@ -129,28 +141,35 @@ def cpu_oracle_step(wl: dict, a: dict, threads: int):
     return acc
 
 
+def cpu_sample(wl: dict, cores: int, Ts: int, seed: int = 1) -> dict:
+    """The bounded CPU sample: one independent segment of Ts steps per core (the op is
+    local in time, so the work per token does not depend on the segment length)."""
+    return make_inputs_np(wl, rows=cores, T=min(wl["T"], Ts), seed=seed)
+
+
 def cpu_baseline(wl: dict, steps: int = 3, budget_s: float = 20.0) -> dict:
-    """Time the oracle on a bounded sample: `rows` batch rows of T_sample steps."""
-    threads = max(1, min(os.cpu_count() or 1, 16))
-    rows = min(wl["B"], threads)
-    Ts = min(wl["T"], 1024)
-    a = make_inputs_np(wl, rows=rows, T=Ts, seed=1)
+    """Time the oracle on a bounded sample spread over every usable host core."""
+    cores = usable_cores()
+    Ts = 512
+    a = cpu_sample(wl, cores, Ts)
     t0 = time.perf_counter()
-    cpu_oracle_step(wl, a, threads)
+    cpu_oracle_step(wl, a, cores)
     first = time.perf_counter() - t0
     n = max(1, min(steps, int(budget_s / max(first, 1e-3))))
     best = first
     for _ in range(n):
         t0 = time.perf_counter()
-        cpu_oracle_step(wl, a, threads)
+        cpu_oracle_step(wl, a, cores)
         best = min(best, time.perf_counter() - t0)
-    toks = rows * Ts
+    toks = a["x"].shape[0] * a["x"].shape[1]
     return {
         "value": toks / best / 1e6,
         "unit": UNIT,
-        "cores": min(threads, rows),
+        "cores": cores,
+        "host_cpus": os.cpu_count(),
         "kind": "port",
-        "sample": f"{rows} batch rows x {Ts} steps of the workload (D={wl['D']}), numpy oracle fwd+bwd, best of {n + 1}",
+        "sample": f"{cores} segments x {a['x'].shape[1]} steps (one per core, D={wl['D']}), numpy restatement of "
+                  f"reference.py fwd+bwd, best of {n + 1}",
     }
 
 
@@ -158,19 +177,19 @@ def run_reference_arm(args, wl: dict) -> None:
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
         return
-    threads = max(1, os.cpu_count() or 1)
-    rows = min(wl["B"], threads)
-    Ts = min(wl["T"], 512)
-    a = make_inputs_np(wl, rows=rows, T=Ts, seed=1)
+    cores = usable_cores()
+    Ts = 512
+    a = cpu_sample(wl, cores, Ts)
     for _ in range(args.warmup):
-        cpu_oracle_step(wl, a, threads)
+        cpu_oracle_step(wl, a, cores)
     times = []
     for _ in range(args.steps):
         t0 = time.perf_counter()
-        cpu_oracle_step(wl, a, threads)
+        cpu_oracle_step(wl, a, cores)
         times.append(time.perf_counter() - t0)
     tot = sum(times)
-    toks = rows * Ts * args.steps
+    rows, Tsamp = a["x"].shape[0], a["x"].shape[1]
+    toks = rows * Tsamp * args.steps
     val = toks / tot / 1e6
     line = {
         "impl": "reference",
@@ -186,13 +205,15 @@ def run_reference_arm(args, wl: dict) -> None:
         "vs_baseline": None,
         "dtype": "f32",
         "data": "synthetic",
-        "config": {"workload": args.workload, **wl, "sample_rows": rows, "sample_T": Ts},
+        "config": {"workload": args.workload, **wl, "sample_segments": rows, "sample_T": Tsamp},
         "cpu_baseline": {
             "value": val,
             "unit": UNIT,
-            "cores": min(threads, rows),
+            "cores": cores,
+            "host_cpus": os.cpu_count(),
             "kind": "port",
-            "sample": f"{rows} batch rows x {Ts} steps per step; numpy restatement of reference.py fwd+bwd",
+            "sample": f"{rows} segments x {Tsamp} steps per step (one per core); numpy restatement of "
+                      "reference.py fwd+bwd",
         },
         "e2e": {"value": val, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
@@ -292,11 +313,195 @@ def _traffic_from_profiles(workload: str):
         return None
 
 
+def device_inputs(wl: dict, dev, seed: int):
+    """Seeded synthetic inputs generated on the device (bf16), with BASELINE's
+    distributions; the shared parameters (U, static_w) use one seed on every rank."""
+    import torch
+
+    B, T, D, W = wl["B"], wl["T"], wl["D"], wl["W"]
+    bf = torch.bfloat16
+    g = torch.Generator(device=dev).manual_seed(seed)
+    gs = torch.Generator(device=dev).manual_seed(7)
+    x = torch.randn(B, T, D, device=dev, generator=g).to(bf).requires_grad_()
+    dy = torch.randn(B, T, D, device=dev, generator=g).to(bf)
+    if wl["kind"] == "lowrank":
+        R = wl["R"]
+        z = torch.randn(B, T, R, device=dev, generator=g).to(bf).requires_grad_()
+        U = (torch.randn(R, W * D, device=dev, generator=gs) / np.sqrt(R)).to(bf).requires_grad_()
+        sw = (torch.rand(W, D, device=dev, generator=gs) - 0.5).to(bf).requires_grad_()
+        return [x, z, U, sw], dy
+    wgt = torch.randn(B, T, wl["H"], W, device=dev, generator=g).to(bf).requires_grad_()
+    sw = torch.randn(W, D, device=dev, generator=gs).to(bf).requires_grad_()
+    return [x, wgt, sw], dy
+
+
+class DeviceStep:
+    """One fwd+bwd step of `fn` on resident inputs, captured in a CUDA graph (eager if
+    capture fails), timed with CUDA events per step with an L2 flush before each."""
+
+    def __init__(self, args, wl, leaves, dy, fn, dev, world, dp_ctx, flush):
+        import torch
+
+        self.args, self.wl, self.leaves, self.dy, self.fn = args, wl, leaves, dy, fn
+        self.dev, self.world, self.dp_ctx, self.flush = dev, world, dp_ctx, flush
+        self.res = bool(wl["residual"])
+        self.graph = None
+        self.graph_error = None
+        with dp_ctx():
+            for _ in range(max(args.warmup, 3)):
+                self.step()
+        torch.cuda.synchronize()
+        if not args.no_graph:
+            try:
+                s = torch.cuda.Stream(device=dev)
+                s.wait_stream(torch.cuda.current_stream(dev))
+                with torch.cuda.stream(s), dp_ctx():
+                    for _ in range(2):
+                        self.step()
+                torch.cuda.current_stream(dev).wait_stream(s)
+                torch.cuda.synchronize()
+                graph = torch.cuda.CUDAGraph()
+                for l in leaves:
+                    l.grad = None
+                with torch.cuda.graph(graph), dp_ctx():
+                    y_static = fn(*leaves, residual=self.res)
+                    y_static.backward(dy)
+                torch.cuda.synchronize()
+                self.graph = graph
+            except Exception as e:  # pragma: no cover - reported in the JSON line
+                self.graph_error = repr(e)[:200]
+
+    def step(self):
+        for l in self.leaves:
+            l.grad = None
+        y = self.fn(*self.leaves, residual=self.res)
+        y.backward(self.dy)
+        return y
+
+    def run_one(self):
+        if self.graph is not None:
+            self.graph.replay()
+        else:
+            with self.dp_ctx():
+                self.step()
+
+    def measure(self, steps: int, local: int) -> dict:
+        """K timed steps (after W untimed), max over ranks; clocks sampled meanwhile."""
+        import torch
+        import torch.distributed as dist
+
+        from dynamic_conv1d_b200 import _lib
+
+        lib = _lib.load()
+        world, dev = self.world, self.dev
+        for _ in range(self.args.warmup):
+            self.run_one()
+        starts = [torch.cuda.Event(enable_timing=True) for _ in range(steps)]
+        ends = [torch.cuda.Event(enable_timing=True) for _ in range(steps)]
+        launches0 = lib.dynconv_launch_count()
+        with ClockSampler(local) as clk:
+            clk.wait_first_sample()
+            if world > 1:
+                dist.barrier()
+            torch.cuda.synchronize()
+            wall0 = time.perf_counter()
+            for i in range(steps):
+                self.flush.zero_()
+                starts[i].record()
+                self.run_one()
+                ends[i].record()
+            torch.cuda.synchronize()
+            wall = time.perf_counter() - wall0
+            launches = lib.dynconv_launch_count() - launches0
+            # The timed region is a few milliseconds, shorter than the 200 ms sampling
+            # period: keep the same step running (untimed) until the sampler has seen
+            # at least 3 samples under this load.  Every replay holds the data-parallel
+            # all-reduce, so all ranks must run the same number of them: each round the
+            # ranks agree (MAX) on whether any of them still needs samples.
+            clk.mark()
+            t_end = time.perf_counter() + 5.0
+            while True:
+                need = clk.samples_since_mark() < 3 and time.perf_counter() < t_end
+                if world > 1:
+                    flag = torch.tensor([1 if need else 0], device=dev, dtype=torch.int32)
+                    dist.all_reduce(flag, op=dist.ReduceOp.MAX)
+                    need = bool(flag.item())
+                if not need:
+                    break
+                for _ in range(20):
+                    self.flush.zero_()
+                    self.run_one()
+                torch.cuda.synchronize()
+        if world > 1:
+            dist.barrier()
+        total_ms = sum(s.elapsed_time(e) for s, e in zip(starts, ends))
+        t = torch.tensor([total_ms], device=dev, dtype=torch.float64)
+        if world > 1:
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        total_ms = float(t.item())
+        # graph replays launch without going through the library: count one step eagerly
+        if self.graph is not None:
+            l0 = lib.dynconv_launch_count()
+            with self.dp_ctx():
+                self.step()
+            torch.cuda.synchronize()
+            launches = (lib.dynconv_launch_count() - l0) * steps
+        return {"total_ms": total_ms, "wall": wall, "launches": launches, "clocks": clk.summary()}
+
+    def release(self):
+        self.graph = None
+
+
+def _dp_ctx_factory(world):
+    import contextlib
+
+    from dynamic_conv1d_b200 import data_parallel
+
+    def dp_ctx():
+        return data_parallel() if world > 1 else contextlib.nullcontext()
+
+    return dp_ctx
+
+
+def sub_workload(args, name: str, wl: dict, dev, world: int, local: int, rank: int, flush, scaling: str) -> dict:
+    """The same device-timed measurement on another BASELINE config (no e2e / CPU leg):
+    value, step roofline fraction, the backward kernel's roofline and the clocks."""
+    import torch
+
+    from dynamic_conv1d_b200 import headwise_dynamic_convolution, lowrank_dynamic_convolution
+
+    fn = lowrank_dynamic_convolution if wl["kind"] == "lowrank" else headwise_dynamic_convolution
+    leaves, dy = device_inputs(wl, dev, seed=100 + rank)
+    ds = DeviceStep(args, wl, leaves, dy, fn, dev, world, _dp_ctx_factory(world), flush)
+    steps = max(5, min(args.steps, 10))
+    m = ds.measure(steps, local)
+    roof = kernel_roofline(args, wl, leaves, dy, fn, flush, dev, workload=name)
+    ds.release()
+    fwd_b, bwd_b = algorithmic_bytes(wl)
+    peak = _peaks()[0]
+    ms = m["total_ms"] / steps
+    out = {
+        "value": world * wl["B"] * wl["T"] * steps / (m["total_ms"] / 1e3) / 1e6,
+        "unit": UNIT,
+        "ms_per_step": ms,
+        "steps": steps,
+        "scaling": scaling,
+        "config": {**wl, "global_batch": wl["B"] * world, "parallelism": f"dp{world}"},
+        "hbm_roofline_frac_step": (fwd_b + bwd_b) / (ms / 1e3) / (peak * 1e9),
+        "roofline": roof,
+        "clocks": m["clocks"],
+        "gpu_launches": m["launches"],
+    }
+    del leaves, dy, ds
+    torch.cuda.empty_cache()
+    return out
+
+
 def run_ours(args, wl: dict) -> None:
     import torch
     import torch.distributed as dist
 
-    from dynamic_conv1d_b200 import _lib, data_parallel, headwise_dynamic_convolution, lowrank_dynamic_convolution
+    from dynamic_conv1d_b200 import headwise_dynamic_convolution, lowrank_dynamic_convolution
 
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
@@ -323,133 +528,43 @@ def run_ours(args, wl: dict) -> None:
     x = dev_t(a["x"], True)
     dy = dev_t(a["dy"])
     if wl["kind"] == "lowrank":
-        z = dev_t(a["z"], True)
-        U = dev_t(a_sw["U"], True)
-        sw = dev_t(a_sw["static_w"], True)
-        leaves = [x, z, U, sw]
+        leaves = [x, dev_t(a["z"], True), dev_t(a_sw["U"], True), dev_t(a_sw["static_w"], True)]
         fn = lowrank_dynamic_convolution
     else:
-        wgt = dev_t(a["weight"], True)
-        sw = dev_t(a_sw["static_w"], True)
-        leaves = [x, wgt, sw]
+        leaves = [x, dev_t(a["weight"], True), dev_t(a_sw["static_w"], True)]
         fn = headwise_dynamic_convolution
-    res = bool(wl["residual"])
-
-    def step():
-        for l in leaves:
-            l.grad = None
-        y = fn(*leaves, residual=res)
-        y.backward(dy)
-        return y
 
     flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
+    dp_ctx = _dp_ctx_factory(world)
 
-    def dp_ctx():
-        import contextlib
-
-        return data_parallel() if world > 1 else contextlib.nullcontext()
-
-    # ---- warm-up (eager), then capture one fwd+bwd step in a CUDA graph
-    with dp_ctx():
-        for _ in range(max(args.warmup, 3)):
-            step()
-    torch.cuda.synchronize()
-    use_graph = not args.no_graph
-    graph = None
-    if use_graph:
-        try:
-            s = torch.cuda.Stream(device=dev)
-            s.wait_stream(torch.cuda.current_stream(dev))
-            with torch.cuda.stream(s), dp_ctx():
-                for _ in range(2):
-                    step()
-            torch.cuda.current_stream(dev).wait_stream(s)
-            torch.cuda.synchronize()
-            graph = torch.cuda.CUDAGraph()
-            for l in leaves:
-                l.grad = None
-            with torch.cuda.graph(graph), dp_ctx():
-                y_static = fn(*leaves, residual=res)
-                y_static.backward(dy)
-            torch.cuda.synchronize()
-        except Exception as e:  # pragma: no cover - reported in the JSON line
-            graph = None
-            use_graph = False
-            graph_error = repr(e)[:200]
-    lib = _lib.load()
-
-    def run_one():
-        if graph is not None:
-            graph.replay()
-        else:
-            with dp_ctx():
-                step()
-
-    # ---- timed region: K steps, per-step CUDA events, L2 flush between steps
-    for _ in range(args.warmup):
-        run_one()
-    starts = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
-    ends = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
-    launches0 = lib.dynconv_launch_count()
-    with ClockSampler(local) as clk:
-        clk.wait_first_sample()
-        if world > 1:
-            dist.barrier()
-        torch.cuda.synchronize()
-        wall0 = time.perf_counter()
-        for i in range(args.steps):
-            flush.zero_()
-            starts[i].record()
-            run_one()
-            ends[i].record()
-        torch.cuda.synchronize()
-        wall = time.perf_counter() - wall0
-        launches = lib.dynconv_launch_count() - launches0
-        # The timed region is a few milliseconds, shorter than the 200 ms sampling
-        # period: keep the same step running (untimed) until the sampler has seen
-        # at least 3 samples under this load.
-        # Every replay holds the data-parallel all-reduce, so all ranks must run
-        # the same number of them: each round the ranks agree (MAX) on whether any
-        # of them still needs samples.
-        clk.mark()
-        t_end = time.perf_counter() + 5.0
-        while True:
-            need = clk.samples_since_mark() < 3 and time.perf_counter() < t_end
-            if world > 1:
-                flag = torch.tensor([1 if need else 0], device=dev, dtype=torch.int32)
-                dist.all_reduce(flag, op=dist.ReduceOp.MAX)
-                need = bool(flag.item())
-            if not need:
-                break
-            for _ in range(20):
-                flush.zero_()
-                run_one()
-            torch.cuda.synchronize()
-    if world > 1:
-        dist.barrier()
-    step_ms = [s.elapsed_time(e) for s, e in zip(starts, ends)]
-    total_ms = sum(step_ms)
-    t = torch.tensor([total_ms], device=dev, dtype=torch.float64)
-    if world > 1:
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-    total_ms = float(t.item())
-    # graph replays launch without going through the library: count one replay eagerly
-    if graph is not None:
-        l0 = lib.dynconv_launch_count()
-        with dp_ctx():
-            step()
-        torch.cuda.synchronize()
-        launches = (lib.dynconv_launch_count() - l0) * args.steps
-
+    # ---- the headline step: fwd+bwd of the metric's config
+    ds = DeviceStep(args, wl, leaves, dy, fn, dev, world, dp_ctx, flush)
+    m = ds.measure(args.steps, local)
+    total_ms = m["total_ms"]
     value = world * ntok * args.steps / (total_ms / 1e3) / 1e6
 
     # ---- dominant kernel: the backward C-ABI call, timed alone (CUDA events)
-    roof = kernel_roofline(args, wl, leaves, dy, fn, flush, dev)
+    roof = kernel_roofline(args, wl, leaves, dy, fn, flush, dev, workload=args.workload)
+    graph_on = ds.graph is not None
+    graph_error = ds.graph_error
+    ds.release()
 
     # ---- e2e through the public API with host buffers
     e2e = None
     if not args.no_e2e:
-        e2e = end_to_end(args, wl, a, a_sw, fn, dev, world, dp_ctx)
+        e2e = end_to_end(args, wl, a, a_sw, fn, dev, world)
+    del leaves, dy, x, a
+    torch.cuda.empty_cache()
+
+    # ---- the other BASELINE configs, device-timed the same way (every rank takes part)
+    subs = {}
+    if not args.no_sub and args.workload == "lowrank" and args.batch is None and args.seq is None:
+        for name in ("headwise_hs32", "headwise_hs1"):
+            subs[name] = sub_workload(args, name, dict(WORKLOADS[name]), dev, world, local, rank, flush, "weak")
+        # B = 64 split over the ranks (strong scaling: the job's work is fixed)
+        cfg5 = dict(WORKLOADS["lowrank_dp"])
+        cfg5["B"] = max(1, 64 // world)
+        subs["lowrank_dp_cfg5"] = sub_workload(args, "lowrank_dp", cfg5, dev, world, local, rank, flush, "strong")
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
@@ -479,29 +594,29 @@ def run_ours(args, wl: dict) -> None:
                 "seq_len": T,
                 "parallelism": f"dp{world}",
                 "l2": "flushed between steps (256 MiB write outside the timed events)",
-                "step": "fwd+bwd, CUDA-graph replay" if graph is not None else "fwd+bwd, eager",
-                "wall_s_timed_region": wall,
+                "step": "fwd+bwd, CUDA-graph replay" if graph_on else "fwd+bwd, eager",
+                "wall_s_timed_region": m["wall"],
                 "hbm_roofline_ms_per_step": (fwd_b + bwd_b) / (_peaks()[0] * 1e9) * 1e3,
                 "hbm_roofline_frac_step": ((fwd_b + bwd_b) / (total_ms / args.steps / 1e3)) / (_peaks()[0] * 1e9),
             },
             "roofline": roof,
-            "clocks": clk.summary(),
-            "gpu_launches": launches,
+            "clocks": m["clocks"],
+            "gpu_launches": m["launches"],
         }
-        if graph is None and use_graph is False and not args.no_graph:
+        if not graph_on and not args.no_graph:
             line["config"]["graph_error"] = graph_error
         if e2e is not None:
             line["e2e"] = e2e
         if cpu is not None:
             line["cpu_baseline"] = cpu
+        if subs:
+            line["workloads"] = subs
         print(json.dumps(line), flush=True)
     if world > 1:
-        if graph is not None:
-            del graph
         dist.destroy_process_group()
 
 
-def kernel_roofline(args, wl, leaves, dy, fn, flush, dev) -> dict:
+def kernel_roofline(args, wl, leaves, dy, fn, flush, dev, workload=None) -> dict:
     """Average duration of the lowrank/headwise backward C-ABI call (main kernel +
     its fixed-order reduction pass) and of the forward call, each bracketed by CUDA
     events on the launching stream, L2 flushed before every launch."""
@@ -582,7 +697,7 @@ def kernel_roofline(args, wl, leaves, dy, fn, flush, dev) -> dict:
         "peak_source": src,
         "unit": "GB/s",
         "frac": ach / peak,
-        "traffic": _traffic_from_profiles(args.workload),
+        "traffic": _traffic_from_profiles(workload or args.workload),
         "algorithmic_bytes_per_launch": bwd_b,
         "ms_per_launch": t_bwd,
         "forward": {"achieved": ach_f, "frac": ach_f / peak, "ms_per_launch": t_fwd, "algorithmic_bytes_per_launch": fwd_b},
@@ -595,14 +710,15 @@ def ctypes_stream(st):
     return ctypes.c_void_p(st.cuda_stream)
 
 
-def end_to_end(args, wl, a, a_sw, fn, dev, world, dp_ctx) -> dict:
+def end_to_end(args, wl, a, a_sw, fn, dev, world) -> dict:
     """Public API with pinned host buffers: H2D of x, z/weight, dy; fwd+bwd; D2H of
     y and every gradient; all inside the CUDA-event-timed region.
 
     The step is pipelined over batch rows on three streams -- uploads of row i+1
     and downloads of row i-1 overlap the fwd+bwd of row i (PCIe is full duplex) --
     and the shared gradients (dU, dstatic_w) accumulate over the rows as autograd
-    does for any split batch; they are copied back once per step."""
+    does for any split batch.  With N ranks the accumulated shared gradients are
+    summed over the ranks by one all-reduce per step, then copied back."""
     import torch
 
     bf = torch.bfloat16
@@ -624,11 +740,11 @@ def end_to_end(args, wl, a, a_sw, fn, dev, world, dp_ctx) -> dict:
     comp = torch.cuda.current_stream(dev)
     s_in, s_out = torch.cuda.Stream(device=dev), torch.cuda.Stream(device=dev)
     rows = wl["B"]
+    shared = [p for p in (U, sw) if p is not None]
 
     def step():
-        if U is not None:
-            U.grad = None
-        sw.grad = None
+        for p in shared:
+            p.grad = None
         for r in range(rows):
             sl = slice(r, r + 1)
             with torch.cuda.stream(s_in):
@@ -641,9 +757,8 @@ def end_to_end(args, wl, a, a_sw, fn, dev, world, dp_ctx) -> dict:
             x.requires_grad_()
             s2.requires_grad_()
             args_ = [x, s2, U, sw] if U is not None else [x, s2, sw]
-            with dp_ctx():
-                y = fn(*args_, residual=res)
-                y.backward(dy)
+            y = fn(*args_, residual=res)
+            y.backward(dy)
             s_out.wait_stream(comp)
             with torch.cuda.stream(s_out):
                 for t in (y, x.grad, s2.grad):
@@ -651,6 +766,17 @@ def end_to_end(args, wl, a, a_sw, fn, dev, world, dp_ctx) -> dict:
                 outs["y"][sl].copy_(y.detach(), non_blocking=True)
                 outs["dx"][sl].copy_(x.grad, non_blocking=True)
                 outs["d2"][sl].copy_(s2.grad, non_blocking=True)
+        if world > 1:
+            # one collective per step: the rank-local sums of the shared gradients
+            import torch.distributed as dist
+
+            flat = torch.cat([p.grad.float().flatten() for p in shared])
+            dist.all_reduce(flat, op=dist.ReduceOp.SUM)
+            off = 0
+            for p in shared:
+                n = p.grad.numel()
+                p.grad.copy_(flat[off:off + n].view_as(p.grad))
+                off += n
         s_out.wait_stream(comp)
         with torch.cuda.stream(s_out):
             outs["dsw"].copy_(sw.grad, non_blocking=True)
@@ -681,8 +807,11 @@ def end_to_end(args, wl, a, a_sw, fn, dev, world, dp_ctx) -> dict:
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
     ms = float(t.item())
     ntok = wl["B"] * wl["T"] * world
+    # PCIe rate per direction seen by this rank (bytes of the step / step time)
     return {"value": ntok / (ms / 1e3) / 1e6, "unit": UNIT, "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
             "ms_per_step": ms, "steps": n, "batches": "best of 3 batches of `steps` steps",
+            "h2d_gbs_per_rank": h2d / (ms / 1e3) / 1e9, "d2h_gbs_per_rank": d2h / (ms / 1e3) / 1e9,
+            "collectives_per_step": 1 if world > 1 else 0,
             "pipeline": f"{rows} batch rows per step, upload / compute / download streams"}
 
 
@@ -698,6 +827,7 @@ def main():
     ap.add_argument("--no-graph", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-sub", action="store_true", help="skip the other BASELINE configs' sub-objects")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3

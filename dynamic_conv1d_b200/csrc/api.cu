@@ -83,6 +83,7 @@ int sm_count() {
 }
 
 unsigned int lr_tc_error_word();
+unsigned int lr_bwd_error_word();
 unsigned int hw_tma_error_word();
 bool hw_tma_supported(int64_t D, int64_t H, int W, int log2hs, int dtype, const void* const* ptrs, int nptrs);
 int hw_tma_partial_rows(int64_t B, int64_t T, int64_t D, int log2hs);
@@ -175,7 +176,7 @@ int dynconv_check_device(void* stream) {
   cudaStream_t st = (cudaStream_t)stream;
   cudaError_t e = cudaStreamSynchronize(st);
   if (e != cudaSuccess) return cuda_status(e, "cudaStreamSynchronize");
-  const unsigned int words[3] = {lr_tc_error_word(), selftest_error_word(), hw_tma_error_word()};
+  const unsigned int words[4] = {lr_tc_error_word(), lr_bwd_error_word(), selftest_error_word(), hw_tma_error_word()};
   for (unsigned int v : words) {
     if (v == 0xFFFFFFFFu) return set_error(DYNCONV_ERR_CUDA, "could not read the device error word");
     if (v != 0) return set_error(DYNCONV_ERR_TIMEOUT, "a device-side bounded wait gave up (site %u)", v);

@@ -157,6 +157,38 @@ __device__ __forceinline__ void store_span(T* __restrict__ p, const float (&v)[N
 
 // ------------------------------------------------------------ PTX wrappers
 
+// Packed fp32 pair arithmetic (sm_100 f32x2 instructions, round to nearest even).
+__device__ __forceinline__ float2 fma2(float2 a, float2 b, float2 c) {
+  float2 d;
+  asm("{\n\t.reg .b64 ra, rb, rc, rd;\n\t"
+      "mov.b64 ra, {%2, %3};\n\tmov.b64 rb, {%4, %5};\n\tmov.b64 rc, {%6, %7};\n\t"
+      "fma.rn.f32x2 rd, ra, rb, rc;\n\tmov.b64 {%0, %1}, rd;\n\t}"
+      : "=f"(d.x), "=f"(d.y)
+      : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y), "f"(c.x), "f"(c.y));
+  return d;
+}
+
+__device__ __forceinline__ float2 add2(float2 a, float2 b) {
+  float2 d;
+  asm("{\n\t.reg .b64 ra, rb, rd;\n\t"
+      "mov.b64 ra, {%2, %3};\n\tmov.b64 rb, {%4, %5};\n\t"
+      "add.rn.f32x2 rd, ra, rb;\n\tmov.b64 {%0, %1}, rd;\n\t}"
+      : "=f"(d.x), "=f"(d.y)
+      : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y));
+  return d;
+}
+
+__device__ __forceinline__ float2 mul2(float2 a, float2 b) {
+  float2 d;
+  asm("{\n\t.reg .b64 ra, rb, rd;\n\t"
+      "mov.b64 ra, {%2, %3};\n\tmov.b64 rb, {%4, %5};\n\t"
+      "mul.rn.f32x2 rd, ra, rb;\n\tmov.b64 {%0, %1}, rd;\n\t}"
+      : "=f"(d.x), "=f"(d.y)
+      : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y));
+  return d;
+}
+
+
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
   return static_cast<uint32_t>(__cvta_generic_to_shared(p));
 }
@@ -183,6 +215,12 @@ __device__ __forceinline__ void fence_proxy_async_smem() {
 
 __device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
   asm volatile("mbarrier.arrive.release.cta.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
+
+// Arrives `count` times at once (count >= 1).
+__device__ __forceinline__ void mbar_arrive_cnt(uint64_t* bar, uint32_t count) {
+  asm volatile("mbarrier.arrive.release.cta.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)), "r"(count)
+               : "memory");
 }
 
 __device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t* bar, uint32_t bytes) {
@@ -231,9 +269,10 @@ __device__ __forceinline__ uint64_t globaltimer_ns() {
 constexpr uint64_t kWaitLimitNs = 1500000000ull;  // 1.5 s
 constexpr uint32_t kWaitSuspendNs = 1000000u;       // longest single suspension, 1 ms
 
-__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, unsigned int site,
-                                          volatile int* abort_flag) {
-  if (mbar_try_wait(bar, parity)) return true;  // fast path: phase already complete
+// Slow path of mbar_wait, kept out of line so that the many wait sites of a
+// warp-specialised kernel stay small in the instruction cache.
+static __device__ __noinline__ bool mbar_wait_slow(uint64_t* bar, uint32_t parity, unsigned int site,
+                                            volatile int* abort_flag) {
   if (*abort_flag) return false;
   const uint64_t t0 = globaltimer_ns();
   for (;;) {
@@ -244,6 +283,12 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, unsign
   atomicCAS(&g_device_error, 0u, site);
   *abort_flag = 1;
   return false;
+}
+
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, unsigned int site,
+                                          volatile int* abort_flag) {
+  if (mbar_try_wait(bar, parity)) return true;  // fast path: phase complete (the try may suspend briefly)
+  return mbar_wait_slow(bar, parity, site, abort_flag);
 }
 
 // TMA tiled 3-D load into shared memory, completion counted on `bar`.
@@ -366,6 +411,28 @@ __device__ __forceinline__ void umma_f16_ts(uint32_t d_tmem, uint32_t a_tmem, ui
       : "memory");
 }
 
+// As umma_f16 / umma_f16_ts with a compile-time accumulate flag (no predicate
+// computation between back-to-back MMAs of an issuing thread).
+template <int ACC>
+__device__ __forceinline__ void umma_f16_c(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_t idesc) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "l"(a_desc), "l"(b_desc), "r"(idesc), "n"(ACC)
+      : "memory");
+}
+
+template <int ACC>
+__device__ __forceinline__ void umma_f16_ts_c(uint32_t d_tmem, uint32_t a_tmem, uint64_t b_desc, uint32_t idesc) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "r"(a_tmem), "l"(b_desc), "r"(idesc), "n"(ACC)
+      : "memory");
+}
+
 // 32 lanes x 8 consecutive 32-bit columns from registers; lane i of the warp writes row (base lane + i).
 __device__ __forceinline__ void tmem_st8(uint32_t taddr, const uint32_t (&v)[8]) {
   asm volatile("tcgen05.st.sync.aligned.32x32b.x8.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8};" ::"r"(taddr),
@@ -434,6 +501,38 @@ __device__ __forceinline__ uint64_t make_smem_desc(uint32_t smem_addr, uint32_t 
   d |= (uint64_t)((sbo >> 4) & 0x3FFFu) << 32;
   d |= (uint64_t)1 << 46;  // descriptor version for sm_100
   // base offset 0, lbo mode 0, layout type 0 (SWIZZLE_NONE)
+  return d;
+}
+
+// Shared-memory matrix descriptor, 128-byte swizzle (the layout a TMA load with
+// CU_TENSOR_MAP_SWIZZLE_128B writes: 16-byte chunk c of 128-byte row r sits at
+// chunk c ^ (r % 8); the pattern repeats every 1024 bytes, so the start address
+// must be 1024-aligned).  MN-major operand: lbo = byte stride between 64-element
+// atoms along M/N, sbo = byte stride between groups of 8 rows along K.
+__device__ __forceinline__ uint64_t make_smem_desc_sw128(uint32_t smem_addr, uint32_t lbo, uint32_t sbo) {
+  uint64_t d = make_smem_desc(smem_addr, lbo, sbo);
+  d |= (uint64_t)2 << 61;  // layout type SWIZZLE_128B
+  return d;
+}
+
+// Byte offset of element (mn, k) in a 128-byte-swizzled MN-major operand whose
+// 64-element atoms are `lbo` bytes apart (rows of 128 bytes, 8-row groups 1024 apart).
+__host__ __device__ __forceinline__ uint32_t mnmajor_sw128_off(int mn, int k, uint32_t lbo) {
+  const uint32_t c = (uint32_t)(mn & 63);
+  return (uint32_t)(mn >> 6) * lbo + (uint32_t)(k >> 3) * 1024u + (uint32_t)(k & 7) * 128u +
+         ((((c >> 3) ^ (uint32_t)(k & 7)) & 7u) << 4) + (c & 7u) * 2u;
+}
+
+// bf16 pair helpers: pack two floats (round to nearest even; exact for values
+// that are already bf16) and the correctly rounded product of two bf16 pairs.
+__device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
+  const __nv_bfloat162 p = __floats2bfloat162_rn(lo, hi);
+  return *reinterpret_cast<const uint32_t*>(&p);
+}
+
+__device__ __forceinline__ uint32_t mul_bf16x2(uint32_t a, uint32_t b) {
+  uint32_t d;
+  asm("mul.rn.bf16x2 %0, %1, %2;" : "=r"(d) : "r"(a), "r"(b));
   return d;
 }
 

@@ -1,0 +1,133 @@
+// lowrank_tc.cuh -- pieces shared by the tcgen05 lowrank forward (lowrank_tc.cu)
+// and backward (lowrank_bwd_tc.cu) kernels, bf16 only.
+//
+// Work split: a tile is 128 channels (one channel block, the MMA M dimension)
+// x 64 timesteps of one batch row.  CTA (dblk, g) of a grid of n_dblk x n_groups
+// owns channel block dblk for the contiguous range of tiles [j0, j1) of group g,
+// tiles numbered b * tiles_row + t0 / 64.  A fixed channel block per CTA means
+// its U block is loaded once, and the CTAs of one tile (one per channel block)
+// run in step, which the backward's cross-CTA dz reduction relies on.
+//
+// z_pack: z rows are 2R bytes (30 at R = 15), which TMA cannot tile (row pitch
+// not a multiple of 16 bytes), so z plus the static rank is first packed as
+// [R_kernel/8][B][T][8] bf16 -- a 4-D box of that lands in shared memory in the
+// no-swizzle K-major operand layout.
+#pragma once
+
+#include "common.cuh"
+
+namespace dynconv {
+namespace lrtc {
+
+constexpr int kBT = 64;   // timesteps per tile
+constexpr int kBD = 128;  // channels per tile (MMA M, TMEM lanes)
+
+struct TileSplit {
+  int n_dblk, n_groups, tiles_row, n_tiles;
+};
+
+inline TileSplit tile_split(int64_t B, int64_t T, int64_t D) {
+  TileSplit sp;
+  sp.n_dblk = (int)((D + kBD - 1) / kBD);
+  sp.tiles_row = (int)((T + kBT - 1) / kBT);
+  sp.n_tiles = (int)(B * sp.tiles_row);
+  int ng = sm_count() / sp.n_dblk;
+  if (ng < 1) ng = 1;
+  if (ng > sp.n_tiles) ng = sp.n_tiles;
+  sp.n_groups = ng;
+  return sp;
+}
+
+__host__ __device__ constexpr uint32_t round1024(uint32_t v) { return (v + 1023u) / 1024u * 1024u; }
+
+inline bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; }
+
+// cuTensorMapEncodeTiled through the runtime's driver entry point (nullptr when
+// the driver does not provide it).
+using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                   const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                   CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+EncodeTiledFn encode_fn();
+
+// 3-D bf16 map over a [B][T][D] tensor: dims (D, T, B), box (box_d, box_t, 1).
+// With swizzle128, box_d must be 64 (128-byte rows) and the destination 1024-aligned.
+int make_btd_map(CUtensorMap* map, const void* base, int64_t B, int64_t T, int64_t D, int box_d, int box_t,
+                 bool swizzle128 = false);
+
+// 4-D bf16 map over z_pack [RKP/8][B][T][8]: dims (8, T, B, RKP/8), box (8, rows, 1, RKP/8).
+// The box lands as [RKP/8][rows][8] (16-byte rows, 8-rank chunks rows*16 bytes apart);
+// rows past T read as zero.
+int make_zpack_map(CUtensorMap* map, const void* base, int64_t B, int64_t T, int rkp, int rows);
+
+size_t zpack_bytes(int64_t B, int64_t T, int rkp);
+int z_pack_launch(const void* z, void* zp, int64_t B, int64_t T, int R, int rkp, bool has_static, cudaStream_t st);
+
+// Loads U_ext for channel block dblk into shared memory: one [128 ch x RKP] K-major
+// no-swizzle block per tap (rank R = static_w when present, zero up to RKP).  The NT
+// calling threads each read up to ceil(W*RKP*16 / NT) 16-byte vectors (8 channels
+// of one (rank, tap) row; D % 8 == 0 on the tensor-core path, so a vector never
+// straddles the end of D), all loads issued before any store.
+template <int W, int RKP, int NT>
+__device__ void load_u_block(uint8_t* us, const __nv_bfloat16* __restrict__ U, const __nv_bfloat16* __restrict__ sw,
+                             int dblk, int D, int R, int tid) {
+  constexpr uint32_t kUTap = (uint32_t)kBD * RKP * 2;
+  constexpr uint32_t kUSbo = (RKP / 8) * 128;
+  constexpr int NV = W * RKP * (kBD / 8);
+  constexpr int PER = (NV + NT - 1) / NT;
+  const int d0 = dblk * kBD;
+  uint4 u[PER];
+#pragma unroll
+  for (int i = 0; i < PER; ++i) {
+    const int e = tid + i * NT;
+    u[i] = make_uint4(0, 0, 0, 0);
+    if (e < NV) {
+      const int v8 = e % (kBD / 8);  // 8-channel group
+      const int r = (e / (kBD / 8)) % RKP;
+      const int w = e / ((kBD / 8) * RKP);
+      const int d = d0 + v8 * 8;
+      if (d < D) {
+        if (r < R) u[i] = __ldg(reinterpret_cast<const uint4*>(U + ((size_t)r * W + w) * D + d));
+        else if (r == R && sw != nullptr) u[i] = __ldg(reinterpret_cast<const uint4*>(sw + (size_t)w * D + d));
+      }
+    }
+  }
+#pragma unroll
+  for (int i = 0; i < PER; ++i) {
+    const int e = tid + i * NT;
+    if (e < NV) {
+      const int v8 = e % (kBD / 8);
+      const int r = (e / (kBD / 8)) % RKP;
+      const int w = e / ((kBD / 8) * RKP);
+      const __nv_bfloat16* h = reinterpret_cast<const __nv_bfloat16*>(&u[i]);
+#pragma unroll
+      for (int k = 0; k < 8; ++k)
+        *reinterpret_cast<__nv_bfloat16*>(us + w * kUTap + kmajor_off(v8 * 8 + k, r, kUSbo, 128)) = h[k];
+    }
+  }
+}
+
+// U^T into tensor memory as the K-major A operand of the weight MMAs: lane = channel,
+// column w*RKP/2 + c of the region holds ranks (2c, 2c+1) of tap w, read from the
+// K-major shared-memory copy (ranks 2c, 2c+1 are adjacent there, one 4-byte load
+// per TMEM word).  Called by one warp per TMEM lane quarter q.
+template <int W, int RKP>
+__device__ __forceinline__ void stage_ut_tmem(const uint8_t* us, uint32_t taddr_region, int q, int lane) {
+  constexpr uint32_t kUTap = (uint32_t)kBD * RKP * 2;
+  constexpr uint32_t kUChunk = (RKP / 8) * 128;
+  const int ch = q * 32 + lane;
+#pragma unroll
+  for (int w = 0; w < W; ++w) {
+#pragma unroll
+    for (int c0 = 0; c0 < RKP / 2; c0 += 8) {
+      uint32_t v[8];
+#pragma unroll
+      for (int i = 0; i < 8; ++i)
+        v[i] = *reinterpret_cast<const uint32_t*>(us + w * kUTap + kmajor_off(ch, 2 * (c0 + i), kUChunk, 128));
+      tmem_st8(taddr_region + ((uint32_t)(q * 32) << 16) + w * (RKP / 2) + c0, v);
+    }
+  }
+  tmem_st_wait();
+}
+
+}  // namespace lrtc
+}  // namespace dynconv

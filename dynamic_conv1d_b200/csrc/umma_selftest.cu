@@ -1,7 +1,8 @@
 // umma_selftest.cu -- a single-CTA tcgen05.mma check of the shared-memory
 // descriptor encodings (no-swizzle K-major and MN-major operands, arbitrary
-// SBO/LBO, row-shifted K-major B) and of the TMEM accumulator layout for
-// M = 64 and M = 128, as used by the lowrank tensor-core kernels.
+// SBO/LBO, row-shifted K-major B), of the 128-byte-swizzled MN-major A operand
+// (the layout a SWIZZLE_128B TMA load writes) and of the TMEM accumulator layout
+// for M = 64 and M = 128, as used by the lowrank tensor-core kernels.
 // Exposed through dynconv_umma_selftest() for the GPU unit tests only.
 #include "common.cuh"
 
@@ -15,19 +16,22 @@ __global__ void __launch_bounds__(128) umma_selftest_kernel(const __nv_bfloat16*
                                                             int a_major, uint32_t a_sbo, uint32_t a_lbo, int b_major,
                                                             uint32_t b_sbo, uint32_t b_lbo, int b_off,
                                                             uint32_t a_bytes, uint32_t ncols) {
-  extern __shared__ __align__(1024) uint8_t smem[];
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = align_smem_1024(smem_raw);
   __shared__ uint64_t bar;
   __shared__ uint32_t tmem_slot;
   __shared__ int abort_flag;
   uint8_t* As = smem;
-  uint8_t* Bs = smem + a_bytes;
+  uint8_t* Bs = smem + (a_bytes + 1023u) / 1024u * 1024u;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
 
   const bool a_tmem = (a_major == 2);  // A staged in TMEM after the D columns
   if (!a_tmem) {
     for (int i = tid; i < M * K; i += blockDim.x) {
       const int m = i / K, k = i % K;
-      const uint32_t off = a_major ? mnmajor_off(m, k, a_sbo, a_lbo) : kmajor_off(m, k, a_sbo, a_lbo);
+      const uint32_t off = a_major == 3 ? mnmajor_sw128_off(m, k, a_lbo)
+                           : a_major   ? mnmajor_off(m, k, a_sbo, a_lbo)
+                                       : kmajor_off(m, k, a_sbo, a_lbo);
       *reinterpret_cast<__nv_bfloat16*>(As + off) = A[i];
     }
   }
@@ -70,14 +74,15 @@ __global__ void __launch_bounds__(128) umma_selftest_kernel(const __nv_bfloat16*
   }
 
   if (tid == 0) {
-    const uint32_t idesc = make_idesc_bf16(M, N, a_tmem ? 0 : a_major, b_major);
+    const uint32_t idesc = make_idesc_bf16(M, N, a_tmem ? 0 : (a_major ? 1 : 0), b_major);
     const uint32_t a0 = smem_u32(As), b0 = smem_u32(Bs) + (uint32_t)b_off * 16u;
     for (int ks = 0; ks < K / 16; ++ks) {
       const uint64_t bd = make_smem_desc(b0 + (uint32_t)ks * 2u * b_lbo, b_lbo, b_sbo);
       if (a_tmem) {
         umma_f16_ts(tbase, tbase + a_col + (uint32_t)ks * 8u, bd, idesc, ks > 0 ? 1u : 0u);
       } else {
-        const uint64_t ad = make_smem_desc(a0 + (uint32_t)ks * 2u * a_lbo, a_lbo, a_sbo);
+        const uint64_t ad = a_major == 3 ? make_smem_desc_sw128(a0 + (uint32_t)ks * 2u * a_sbo, a_lbo, a_sbo)
+                                         : make_smem_desc(a0 + (uint32_t)ks * 2u * a_lbo, a_lbo, a_sbo);
         umma_f16(tbase, ad, bd, idesc, ks > 0 ? 1u : 0u);
       }
     }
@@ -123,9 +128,13 @@ int umma_selftest_launch(const void* A, const void* B, float* D, int M, int N, i
   if ((a_sbo | a_lbo | b_sbo | b_lbo) & 15) return set_error(DYNCONV_ERR_ALIGN, "selftest: strides must be 16-byte multiples");
   if (a_major == 2 && (M != 128 || N + K / 2 > 256))
     return set_error(DYNCONV_ERR_SHAPE, "selftest: A in TMEM needs M = 128 and N + K/2 <= 256");
-  const uint32_t abytes = a_major == 2 ? 128u : span_bytes(a_major, M, K, (uint32_t)a_sbo, (uint32_t)a_lbo);
+  if (a_major == 3 && (a_sbo != 1024 || a_lbo % 1024 != 0 || a_lbo < (K + 7) / 8 * 1024))
+    return set_error(DYNCONV_ERR_SHAPE, "selftest: swizzled A needs SBO = 1024 and LBO a multiple of 1024 past its rows");
+  const uint32_t abytes = a_major == 2   ? 128u
+                          : a_major == 3 ? (uint32_t)((M + 63) / 64) * (uint32_t)a_lbo
+                                         : span_bytes(a_major, M, K, (uint32_t)a_sbo, (uint32_t)a_lbo);
   const uint32_t bbytes = span_bytes(b_major, Nb, K, (uint32_t)b_sbo, (uint32_t)b_lbo);
-  const uint32_t smem = abytes + bbytes;
+  const uint32_t smem = (abytes + 1023u) / 1024u * 1024u + bbytes;
   if (smem > 200 * 1024) return set_error(DYNCONV_ERR_SHAPE, "selftest: operands need %u bytes of smem", smem);
   uint32_t ncols = 32;
   while (ncols < (uint32_t)N + (a_major == 2 ? (uint32_t)K / 2 : 0u)) ncols <<= 1;

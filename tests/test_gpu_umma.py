@@ -37,6 +37,16 @@ CASES = {
     "tmemA_dx_shift2": (128, 32, 16, 72, 2, 0, 0, 0, 128, 72 * 16, 2),
     "tmemA_dU_R16": (128, 16, 64, 16, 2, 0, 0, 1, 72 * 16, 128, 0),
     "tmemA_dU_R32": (128, 32, 64, 32, 2, 0, 0, 1, 72 * 16, 128, 0),
+    # backward, per 16-step quarter: weight MMA (N = 16, z rows from 16i + w) and dU MMA (K = 16)
+    "tmemA_q_shift3": (128, 16, 16, 72, 2, 0, 0, 0, 128, 72 * 16, 3),
+    "tmemA_q_shift51": (128, 16, 32, 72, 2, 0, 0, 0, 128, 72 * 16, 51),
+    "tmemA_q_dU_R16": (128, 16, 16, 16, 2, 0, 0, 1, 72 * 16, 128, 0),
+    "tmemA_q_dU_R32": (128, 32, 16, 32, 2, 0, 0, 1, 72 * 16, 128, 0),
+    # 128-byte-swizzled MN-major A (a_major = 3): a 16-row block of a SWIZZLE_128B TMA
+    # tile, 64-channel atoms LBO apart -- the backward's transposing MMA (B = identity)
+    "sw128_transpose": (128, 16, 16, 16, 3, 1024, 2048, 0, 128, 256, 0),
+    "sw128_K32": (128, 32, 32, 32, 3, 1024, 4096, 0, 128, 512, 0),
+    "sw128_M64": (64, 16, 16, 16, 3, 1024, 2048, 0, 128, 256, 0),
 }
 
 
@@ -56,3 +66,19 @@ def test_umma_layout(name, cuda_device):
     _lib.check_device(A)
     ref = A.float() @ B.float()[:, off:off + N]
     torch.testing.assert_close(D, ref, atol=1e-3, rtol=1e-3)
+
+
+def test_transpose_is_exact(cuda_device):
+    """The identity MMA used to transpose dy/x tiles returns every bf16 value exactly."""
+    M, N, K = 128, 16, 16
+    g = torch.Generator(device="cuda").manual_seed(5)
+    A = (torch.randn(M, K, device="cuda", generator=g) * 1e3).to(torch.bfloat16)
+    B = torch.eye(K, N, device="cuda").to(torch.bfloat16)
+    D = torch.full((M, N), float("nan"), device="cuda", dtype=torch.float32)
+    lib = _lib.load()
+    _lib.check(lib.dynconv_umma_selftest(
+        ctypes.c_void_p(A.data_ptr()), ctypes.c_void_p(B.data_ptr()), ctypes.c_void_p(D.data_ptr()),
+        M, N, K, K, 3, 1024, 2048, 0, 128, 256, 0, _lib.stream_of(A),
+    ))
+    _lib.check_device(A)
+    assert torch.equal(D, A.float())
