@@ -56,18 +56,19 @@ using namespace lrtc;
 constexpr int kQ = 16;                 // steps per quarter
 constexpr int kQPT = kBT / kQ;         // quarters per tile
 constexpr int kBlkPT = kQPT + 1;       // transposed blocks per tile and tensor
-constexpr int kTRing = 4;              // tensor-memory block ring
 constexpr int kZRows = 72;             // z rows t0 .. t0+71 (64 + W-1, whole core matrices)
 constexpr int kCtl = 8;                // control warps (producer + seven MMA issuers)
 constexpr int kEpi = 8;                // epilogue warps: two teams of four (one per TMEM lane quarter)
 constexpr int kThreads = 32 * (kCtl + kEpi);
 
+
 template <int W, int RKP>
 struct BwdCfg {
   static constexpr int kRKP = RKP;
-  static constexpr bool kPT = (RKP == 16);  // P^T for MMA-2 held in tensor memory
+  static constexpr bool kPT = false;        // MMA-2 reads P from shared memory
   static constexpr int NP = 2;              // P buffers (MMA-3 of one tile overlaps the next)
-  static constexpr int S = (RKP == 16) ? 6 : 4;  // shared-memory ring of (dy, x) block pairs
+  static constexpr int S = (RKP == 16) ? 8 : 4;  // shared-memory ring of (dy, x) block pairs
+  static constexpr int kTRing = (RKP == 16) ? 8 : 4;  // tensor-memory block ring (dyT / xT slots)
   // shared memory (bytes from the 1024-aligned base)
   static constexpr uint32_t kHalf = kQ * 128;     // 16 rows x 64 channels (one swizzle atom column)
   static constexpr uint32_t kBlk = 2 * kHalf;     // 128 channels
@@ -80,9 +81,9 @@ struct BwdCfg {
   static constexpr uint32_t kOffP = kOffRing + S * kSlot;
   static constexpr uint32_t kOffU = kOffP + NP * W * kPTap;
   static constexpr uint32_t kOffZ = round1024(kOffU + W * kUTap);
-  static constexpr uint32_t kDxWarp = kQ * 32 * 2;  // [16 steps][32 ch] bf16 sub-tile
+  static constexpr uint32_t kDxWarp = kQ * 32 * 2;  // [16 steps][32 ch] bf16 sub-tile (dx transpose)
   static constexpr uint32_t kOffDx = kOffZ + 2 * kZStride;
-  static constexpr uint32_t kOffI = kOffDx + kEpi * 2 * kDxWarp;
+  static constexpr uint32_t kOffI = kOffDx + kEpi * kDxWarp;
   static constexpr uint32_t kTotal = kOffI + 512 + 1024;  // + alignment slack
   // operand strides
   static constexpr uint32_t kUChunk = (RKP / 8) * 128;  // U: next 8 channels
@@ -93,12 +94,12 @@ struct BwdCfg {
   static constexpr uint32_t kColAcc = 0;
   static constexpr uint32_t kColDyT = 2 * kAcc;
   static constexpr uint32_t kColXT = kColDyT + kTRing * kQ;
-  static constexpr uint32_t kColUA = kColXT + kTRing * kQ;
+
   static constexpr uint32_t kPTSlot = W * 8;           // P^T of one quarter: W taps x 16 steps (bf16 pairs)
-  static constexpr uint32_t kColPT = kColUA + W * RKP / 2;
+  static constexpr uint32_t kColPT = kColXT + kTRing * kQ;
   static constexpr uint32_t kColDU = kColPT + (kPT ? 4 * kPTSlot : 0);
-  static constexpr uint32_t kColDZ = kColDU + W * RKP;  // two MMA-3 accumulators x RKP, M = 64 layout
-  static constexpr uint32_t kCols = kColDZ + 2 * RKP;
+  static constexpr uint32_t kColDZ = kColDU + W * RKP;  // 2 buffers x 2 MMA-3 accumulators x RKP, M = 64 layout
+  static constexpr uint32_t kCols = kColDZ + 4 * RKP;
   static_assert(kCols <= 512, "tensor-memory budget");
   static_assert(kTotal <= 232448 - 1024, "shared-memory budget (227 KB per CTA, static part aside)");
 };
@@ -149,17 +150,17 @@ __device__ __forceinline__ void issue_mma2(uint32_t du, uint32_t pt, uint64_t ad
 template <int W, int RKP>
 __global__ void __launch_bounds__(kThreads, 1)
     lr_bwd_tc_kernel(const __grid_constant__ CUtensorMap dymap, const __grid_constant__ CUtensorMap xmap,
-                     const __grid_constant__ CUtensorMap zmap, const __grid_constant__ CUtensorMap dxmap,
-                     const __nv_bfloat16* __restrict__ U, const __nv_bfloat16* __restrict__ sw, __nv_bfloat16* __restrict__ dz, float* __restrict__ dzp, int* __restrict__ grp_done,
+                     const __grid_constant__ CUtensorMap zmap, const __nv_bfloat16* __restrict__ U,
+                     const __nv_bfloat16* __restrict__ sw, __nv_bfloat16* __restrict__ dx, __nv_bfloat16* __restrict__ dz, float* __restrict__ dzp, int* __restrict__ grp_done,
                      float* __restrict__ dUp, float* __restrict__ dU_f32, __nv_bfloat16* __restrict__ dU,
-                     __nv_bfloat16* __restrict__ dsw, TileSplit sp, int T, int D, int R, int Rk, int residual) {
+                     __nv_bfloat16* __restrict__ dsw, TileSplit sp, int T, int D, int R, int Rk, int residual, int tma4) {
   using L = BwdCfg<W, RKP>;
-  constexpr int S = L::S, NP = L::NP;
+  constexpr int S = L::S, NP = L::NP, kTRing = L::kTRing;
   constexpr int kW0 = (W + 1) / 2;  // taps [0, kW0) go to the first issuer of a split stream
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = align_smem_1024(smem_raw);
   __shared__ uint64_t rfull[S], rempty[S], zfull[2], zempty[2], tfull[kTRing], tfree[kTRing], accfull[2],
-      accempty[2], pf[4], ptempty[4], pe[NP], dzf, dze, du_bar;
+      accempty[2], pf[4], ptempty[4], pe[NP], dzf[2], dze[2], du_bar;
   __shared__ uint32_t tmem_slot;
   __shared__ int abort_flag;
   __shared__ int grp_ok;
@@ -193,8 +194,10 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(&ptempty[c], 2);
     }
     for (int p = 0; p < NP; ++p) mbar_init(&pe[p], L::kPT ? 2 : 4);
-    mbar_init(&dzf, 2);
-    mbar_init(&dze, kEpi);
+    for (int h = 0; h < 2; ++h) {
+      mbar_init(&dzf[h], 2);
+      mbar_init(&dze[h], kEpi);
+    }
     mbar_init(&du_bar, 2);
     abort_flag = 0;
     fence_barrier_init();
@@ -203,7 +206,6 @@ __global__ void __launch_bounds__(kThreads, 1)
     prefetch_tensormap(&dymap);
     prefetch_tensormap(&xmap);
     prefetch_tensormap(&zmap);
-    prefetch_tensormap(&dxmap);
   }
   __syncthreads();  // barriers initialised: the producer starts its loads at once
   uint32_t tmem = 0;
@@ -227,7 +229,6 @@ __global__ void __launch_bounds__(kThreads, 1)
     named_bar_sync(2, kNonProducer);
     tc_fence_after();
     tmem = tmem_slot;
-    if (warp >= kCtl && warp < kCtl + 4) stage_ut_tmem<W, RKP>(smem + L::kOffU, tmem + L::kColUA, warp & 3, lane);
     tc_fence_before();
     named_bar_sync(2, kNonProducer);
     tc_fence_after();
@@ -251,10 +252,15 @@ __global__ void __launch_bounds__(kThreads, 1)
           uint8_t* slot = smem + L::kOffRing + m * L::kSlot;
           mbar_arrive_expect_tx(&rfull[m], L::kSlot);
           // dy block bb: steps t0 + 16bb ..; x block bb: steps t0 - 16 + 16bb .. (zero fill outside [0, T))
-          tma_load_3d(slot, &dymap, &rfull[m], d0, t0 + kQ * bb, b, pol);
-          tma_load_3d(slot + L::kHalf, &dymap, &rfull[m], d0 + 64, t0 + kQ * bb, b, pol);
-          tma_load_3d(slot + L::kBlk, &xmap, &rfull[m], d0, t0 - kQ + kQ * bb, b, pol);
-          tma_load_3d(slot + L::kBlk + L::kHalf, &xmap, &rfull[m], d0 + 64, t0 - kQ + kQ * bb, b, pol);
+          if (tma4) {  // both 64-channel halves in one box
+            tma_load_4d(slot, &dymap, &rfull[m], 0, t0 + kQ * bb, d0 / 64, b, pol);
+            tma_load_4d(slot + L::kBlk, &xmap, &rfull[m], 0, t0 - kQ + kQ * bb, d0 / 64, b, pol);
+          } else {
+            tma_load_3d(slot, &dymap, &rfull[m], d0, t0 + kQ * bb, b, pol);
+            tma_load_3d(slot + L::kHalf, &dymap, &rfull[m], d0 + 64, t0 + kQ * bb, b, pol);
+            tma_load_3d(slot + L::kBlk, &xmap, &rfull[m], d0, t0 - kQ + kQ * bb, b, pol);
+            tma_load_3d(slot + L::kBlk + L::kHalf, &xmap, &rfull[m], d0 + 64, t0 - kQ + kQ * bb, b, pol);
+          }
         }
         if (!ok) break;
       }
@@ -285,10 +291,11 @@ __global__ void __launch_bounds__(kThreads, 1)
   } else if (warp == 2 || warp == 3) {
     // ------------------------------------------------------------ MMA-1 (weights) of one team's quarters
     // Before issuing it also waits for everything else the team's epilogue needs for
-    // the quarter -- the two transposed blocks, a free P^T slot, a free P buffer --
-    // so accfull alone tells the epilogue that the quarter is ready.
+    // the quarter -- the two transposed blocks, a free P buffer -- so accfull alone
+    // tells the epilogue that the quarter is ready.
     const int team = warp - 2;
-    const uint32_t idesc1 = make_idesc_bf16(kBD, kQ, 0, 0);  // A = U^T (TMEM), B = z (K-major)
+    const uint32_t idesc1 = make_idesc_bf16(kBD, kQ, 0, 0);  // A = U^T (K-major, shared), B = z (K-major)
+    const uint64_t ud1 = make_smem_desc(smem_u32(smem + L::kOffU), 128, L::kUChunk);
     const uint64_t zdesc0 = make_smem_desc(smem_u32(smem + L::kOffZ), L::kZChunk, 128);
     const uint32_t acc = tmem + L::kColAcc + team * L::kAcc;
     for (int Q = team; Q < nq; Q += 2) {
@@ -298,7 +305,6 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (!mbar_wait(&accempty[team], ((Q >> 1) & 1) ^ 1, kErrWaitMma, &abort_flag)) break;
       if (!mbar_wait(&tfull[nbA % kTRing], (nbA / kTRing) & 1, kErrWaitMma, &abort_flag)) break;
       if (!mbar_wait(&tfull[(nbA + 1) % kTRing], ((nbA + 1) / kTRing) & 1, kErrWaitMma, &abort_flag)) break;
-      if (L::kPT && !mbar_wait(&ptempty[Q & 3], ((Q >> 2) & 1) ^ 1, kErrWaitMma, &abort_flag)) break;
       if (i < 2 && !mbar_wait(&pe[p], ((k / NP) & 1) ^ 1, kErrWaitMma, &abort_flag)) break;
       tc_fence_after();
       if (lane == 0) {
@@ -309,10 +315,10 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
           for (int ks = 0; ks < RKP / 16; ++ks)
             if (ks == 0)
-              umma_f16_ts_c<0>(acc + w * kQ, tmem + L::kColUA + w * (RKP / 2), zd + (uint64_t)((w * 16) >> 4), idesc1);
+              umma_f16_c<0>(acc + w * kQ, ud1 + (uint64_t)((w * L::kUTap) >> 4), zd + (uint64_t)((w * 16) >> 4), idesc1);
             else
-              umma_f16_ts_c<1>(acc + w * kQ, tmem + L::kColUA + w * (RKP / 2) + ks * 8,
-                               zd + (uint64_t)((w * 16 + ks * 2 * L::kZChunk) >> 4), idesc1);
+              umma_f16_c<1>(acc + w * kQ, ud1 + (uint64_t)((w * L::kUTap + ks * 256) >> 4),
+                            zd + (uint64_t)((w * 16 + ks * 2 * L::kZChunk) >> 4), idesc1);
         }
         umma_commit(&accfull[team]);
         if (i >= kQPT - 2) umma_commit(&zempty[k & 1]);  // this issuer's last read of z tile k
@@ -352,19 +358,20 @@ __global__ void __launch_bounds__(kThreads, 1)
     const uint64_t pd0 = make_smem_desc(smem_u32(smem + L::kOffP), L::kPChunk, 128);
     const uint64_t ud0 = make_smem_desc(smem_u32(smem + L::kOffU), L::kUChunk, 128);
     const uint32_t idesc3 = make_idesc_bf16(64, RKP, 1, 1);  // A = P (MN-major), B = U (MN-major)
-    const uint32_t dacc = tmem + L::kColDZ + half * RKP;
+    const uint32_t dacc0 = tmem + L::kColDZ + half * RKP;
     for (int k = 0; k < n; ++k) {
       const int p = k % NP;
       bool ok = true;
       for (int i = 0; i < kQPT && ok; ++i) ok = mbar_wait(&pf[(kQPT * k + i) & 3], ((kQPT * k + i) >> 2) & 1, kErrWaitMma, &abort_flag);
       if (!ok) break;
-      if (!mbar_wait(&dze, (k & 1) ^ 1, kErrWaitMma, &abort_flag)) break;
+      if (!mbar_wait(&dze[k & 1], ((k >> 1) & 1) ^ 1, kErrWaitMma, &abort_flag)) break;
       tc_fence_after();
       if (lane == 0) {
         const uint64_t ad0 = pd0 + (uint64_t)((p * W * L::kPTap) >> 4);
+        const uint32_t dacc = dacc0 + (k & 1) * 2 * RKP;
         if (half == 0) issue_mma3<0, kW0, L>(dacc, ad0, ud0, idesc3);
         else issue_mma3<kW0, W, L>(dacc, ad0, ud0, idesc3);
-        umma_commit(&dzf);
+        umma_commit(&dzf[k & 1]);
         umma_commit(&pe[p]);
       }
       __syncwarp();
@@ -378,9 +385,9 @@ __global__ void __launch_bounds__(kThreads, 1)
     const bool dok = d0 + ch < D;
     const uint32_t lane_base = (uint32_t)(q * 32) << 16;
     const uint32_t ta = tmem + lane_base;
-    const uint64_t pol_dx = policy_evict_first();
     uint8_t* const pch = smem + L::kOffP + kmajor_off(ch, 0, L::kPChunk, 128);  // this channel's P column
-    __nv_bfloat16* const stage0 = reinterpret_cast<__nv_bfloat16*>(smem + L::kOffDx + e * 2 * L::kDxWarp);
+    __nv_bfloat16* const st = reinterpret_cast<__nv_bfloat16*>(smem + L::kOffDx + e * L::kDxWarp);
+    const int ccol = d0 + q * 32 + (lane & 3) * 8;  // first channel of this lane's 16-byte dx pieces
     bool dead = false;
 
     // dz partial of tile kk (M = 64 layout: lanes 0..15 of quarter q hold steps
@@ -388,15 +395,16 @@ __global__ void __launch_bounds__(kThreads, 1)
     // MMA-3 accumulators are added) -> workspace
     auto dz_readout = [&](int kk) {
       const int tile = j0 + kk;
-      if (!dead) dead = !mbar_wait(&dzf, kk & 1, kErrWaitEpilogue, &abort_flag);
+      if (!dead) dead = !mbar_wait(&dzf[kk & 1], (kk >> 1) & 1, kErrWaitEpilogue, &abort_flag);
       tc_fence_after();
       constexpr int NC = RKP / 2;
       constexpr int NACC = W > 1 ? 2 : 1;
       float v[NC], v2[NC];
       const int c0 = team * NC;
       if (!dead) {
-        tmem_ld_n<NC>(ta + L::kColDZ + c0, v);
-        if constexpr (NACC > 1) tmem_ld_n<NC>(ta + L::kColDZ + RKP + c0, v2);
+        const uint32_t dzc = ta + L::kColDZ + (kk & 1) * 2 * RKP + c0;
+        tmem_ld_n<NC>(dzc, v);
+        if constexpr (NACC > 1) tmem_ld_n<NC>(dzc + RKP, v2);
         tmem_ld_wait();
         if constexpr (NACC > 1) {
 #pragma unroll
@@ -405,7 +413,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive(&dze);
+      if (lane == 0) mbar_arrive(&dze[kk & 1]);
       if (!dead && lane < 16) {
         float* dst = dzp + (((size_t)dblk * sp.n_tiles + tile) * kBT + 16 * q + lane) * RKP + c0;
 #pragma unroll
@@ -420,7 +428,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       const int nbA = kBlkPT * k + i, cA = nbA % kTRing, cB = (nbA + 1) % kTRing;
       if (!dead) dead = !mbar_wait(&accfull[team], it & 1, kErrWaitEpilogue, &abort_flag);
       tc_fence_after();
-      // acc[w][j]: weights of tap w at step 16i + j; dy(m): dy at step 16i + m (m < 20);
+      // acc[w][j]: weights of tap w at step 16i + j0h + j; dy(m): dy at step 16i + m (m < 20);
       // xv(m): x at step 16i - 4 + m (m < 20).  Quarter-relative rows: dy block i holds
       // rows 0..15, dy block i+1 rows 16..31; x block i rows -16..-1, x block i+1 rows 0..15.
       float acc[W][8], dyA[16], dyB[4], xA[4], xB[16];
@@ -435,8 +443,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       auto dyv = [&](int m) -> float { return m < 16 ? dyA[m] : dyB[m - 16]; };
       auto xv = [&](int m) -> float { return m < 4 ? xA[m] : xB[m - 4]; };
-      __nv_bfloat16* st = stage0 + (it & 1) * (L::kDxWarp / 2);
-      // dx[j] = sum_w acc_w[j] dy[j+w] (+ dy[j]) for steps j0 .. j0+7 -> shared sub-tile
+      // dx[j] = sum_w acc_w[j] dy[j+w] (+ dy[j]) for steps j0h .. j0h+7 -> shared sub-tile
       auto dx_half = [&](int j0h) {
 #pragma unroll
         for (int jj = 0; jj < 8; ++jj) {
@@ -448,8 +455,6 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
       };
       if (!dead) {
-        if (lane == 0) bulk_wait_group_read<1>();  // the store of two rounds ago has read this buffer
-        __syncwarp();
         dx_half(0);
 #pragma unroll
         for (int w = 0; w < W; ++w) tmem_ld8(ta + L::kColAcc + team * L::kAcc + w * kQ + 8, acc[w]);
@@ -464,32 +469,44 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       if (!dead) {
         dx_half(8);
-        fence_proxy_async_smem();
         __syncwarp();
-        if (lane == 0) {
-          tma_store_3d(&dxmap, st, d0 + q * 32, t0 + kQ * i, b, pol_dx);
-          bulk_commit_group();
+        // the warp's [16 steps][32 ch] sub-tile, read back as 16-byte row pieces: lane l
+        // stores channels ccol.. of steps l/4 and l/4 + 8 (64 contiguous bytes per 4 lanes)
+        if (ccol < D) {
+#pragma unroll
+          for (int h = 0; h < 2; ++h) {
+            const int r = (lane >> 2) + 8 * h, t = t0 + kQ * i + r;
+            const uint4 v = *reinterpret_cast<const uint4*>(st + r * 32 + (lane & 3) * 8);
+            if (t < T) *reinterpret_cast<uint4*>(dx + ((size_t)b * T + t) * D + ccol) = v;
+          }
         }
-        // ---- P_w = bf16(dy * x_{t-w}) as (step, step+1) pairs -> shared memory (dz MMA)
-        // and, at R_kernel = 16, tensor memory (dU MMA)
-        uint32_t dy2[kQ / 2], x2[20];
+        __syncwarp();  // the sub-tile is rewritten by the next quarter
+        // ---- P_w = bf16(dy * x_{t-w}) as (step, step+1) pairs -> shared memory (dz and dU MMAs)
+        uint32_t dy2[kQ / 2];
 #pragma unroll
         for (int pp = 0; pp < kQ / 2; ++pp) dy2[pp] = pack_bf16x2(dyv(2 * pp), dyv(2 * pp + 1));
-#pragma unroll
-        for (int m = 4 - (W - 1); m <= 18; ++m) x2[m] = pack_bf16x2(xv(m), xv(m + 1));
         uint8_t* pbuf = pch + p * W * L::kPTap + (2 * i) * 128;
+        // tap w pairs step (2pp, 2pp+1) of dy with x rows (2pp-w, 2pp+1-w), i.e. xv pair
+        // m = 2pp + 4 - w: even taps use even m, odd taps odd m -- one parity at a time
 #pragma unroll
-        for (int w = 0; w < W; ++w) {
-          uint32_t pk[8];
+        for (int par = 0; par < 2; ++par) {
+          uint32_t xp[10];  // xp[c] = (xv(2c + par), xv(2c + par + 1))
 #pragma unroll
-          for (int pp = 0; pp < 8; ++pp) pk[pp] = mul_bf16x2(dy2[pp], x2[2 * pp + 4 - w]);
-          *reinterpret_cast<uint4*>(pbuf + w * L::kPTap) = make_uint4(pk[0], pk[1], pk[2], pk[3]);
-          *reinterpret_cast<uint4*>(pbuf + w * L::kPTap + 128) = make_uint4(pk[4], pk[5], pk[6], pk[7]);
-          if constexpr (L::kPT) tmem_st8(ta + L::kColPT + (Q & 3) * L::kPTSlot + w * 8, pk);
+          for (int c = 0; c < 10; ++c) {
+            const int m = 2 * c + par;
+            xp[c] = (m >= 4 - (W - 1) && m <= 18) ? pack_bf16x2(xv(m), xv(m + 1)) : 0u;
+          }
+#pragma unroll
+          for (int w = par; w < W; w += 2) {
+            uint32_t pk[8];
+#pragma unroll
+            for (int pp = 0; pp < 8; ++pp) pk[pp] = mul_bf16x2(dy2[pp], xp[(2 * pp + 4 - w - par) >> 1]);
+            *reinterpret_cast<uint4*>(pbuf + w * L::kPTap) = make_uint4(pk[0], pk[1], pk[2], pk[3]);
+            *reinterpret_cast<uint4*>(pbuf + w * L::kPTap + 128) = make_uint4(pk[4], pk[5], pk[6], pk[7]);
+          }
         }
       }
       fence_proxy_async_smem();
-      if constexpr (L::kPT) tmem_st_wait();
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&pf[Q & 3]);
@@ -508,8 +525,6 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
     }
     if (n >= 1) dz_readout(n - 1);
-    if (lane == 0) bulk_wait_group<0>();
-    __syncwarp();
     // dU partial of this CTA: TMEM (lane = channel) -> dUp[g][r][w*D + d0 + ch]
     if (!dead) dead = !mbar_wait(&du_bar, 0, kErrWaitTail, &abort_flag);
     tc_fence_after();
@@ -565,8 +580,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       const int tile = j0 + (int)(st / kBT), tok = (int)(st % kBT);
       const int b = tile / sp.tiles_row, t = (tile % sp.tiles_row) * kBT + tok;
       float4 a4 = make_float4(0.f, 0.f, 0.f, 0.f);
-#pragma unroll 16
-      for (int k2 = 0; k2 < sp.n_dblk; ++k2) {  // all partial loads in flight, summed in order
+#pragma unroll 4
+      for (int k2 = 0; k2 < sp.n_dblk; ++k2) {  // partial loads in flight, summed in order
         const float4 f =
             __ldcg(reinterpret_cast<const float4*>(dzp + (((size_t)k2 * sp.n_tiles + tile) * kBT + tok) * RKP) + rq);
         a4.x += f.x;
@@ -613,7 +628,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int64_t lo = n4 * blockIdx.x / gridDim.x, hi = n4 * (blockIdx.x + 1) / gridDim.x;
     for (int64_t i = lo + threadIdx.x; i < hi; i += blockDim.x) {
       float4 a4 = make_float4(0.f, 0.f, 0.f, 0.f);
-#pragma unroll 8
+#pragma unroll 4
       for (int gg = 0; gg < sp.n_groups; ++gg) {
         const float4 f = __ldcg(reinterpret_cast<const float4*>(dUp) + (size_t)gg * n4 + i);
         a4.x += f.x;
@@ -672,13 +687,18 @@ int launch_bwd(const void* x, const void* z, const void* U, const void* sw, cons
                float* dU_f32, void* dU, void* dsw, void* wsp, int64_t B, int64_t T, int64_t D, int R, int Rk,
                int residual, cudaStream_t st) {
   using L = BwdCfg<W, RKP>;
-  CUtensorMap dymap, xmap, zmap, dxmap;
+  CUtensorMap dymap, xmap, zmap;
   int s;
   const TileSplit sp = tile_split(B, T, D);
   BwdWorkspace ws = bwd_workspace(wsp, B, T, D, Rk, W);
-  if ((s = make_btd_map(&dymap, dy, B, T, D, 64, kQ, true))) return s;
-  if ((s = make_btd_map(&xmap, x, B, T, D, 64, kQ, true))) return s;
-  if ((s = make_btd_map(&dxmap, dx, B, T, D, 32, kQ))) return s;  // per-warp [16 steps][32 ch] stores
+  const int tma4 = D % 64 == 0 ? 1 : 0;
+  if (tma4) {
+    if ((s = make_btd4_map(&dymap, dy, B, T, D, kQ))) return s;
+    if ((s = make_btd4_map(&xmap, x, B, T, D, kQ))) return s;
+  } else {
+    if ((s = make_btd_map(&dymap, dy, B, T, D, 64, kQ, true))) return s;
+    if ((s = make_btd_map(&xmap, x, B, T, D, 64, kQ, true))) return s;
+  }
   if ((s = make_zpack_map(&zmap, ws.zp, B, T, RKP, kZRows))) return s;
   if ((s = z_pack_launch(z, ws.zp, B, T, R, RKP, sw != nullptr, st))) return s;
   cudaError_t e = cudaMemsetAsync(ws.cnt, 0, (size_t)(sp.n_groups + 1) * sizeof(int), st);
@@ -702,9 +722,9 @@ int launch_bwd(const void* x, const void* z, const void* U, const void* sw, cons
   attr[0].val.cooperative = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  e = cudaLaunchKernelEx(&cfg, lr_bwd_tc_kernel<W, RKP>, dymap, xmap, zmap, dxmap, (const __nv_bfloat16*)U,
-                         (const __nv_bfloat16*)sw, (__nv_bfloat16*)dz, ws.dzp, ws.cnt, ws.dUp, dU_f32,
-                         (__nv_bfloat16*)dU, (__nv_bfloat16*)(sw ? dsw : nullptr), sp, (int)T, (int)D, R, Rk, residual);
+  e = cudaLaunchKernelEx(&cfg, lr_bwd_tc_kernel<W, RKP>, dymap, xmap, zmap, (const __nv_bfloat16*)U,
+                         (const __nv_bfloat16*)sw, (__nv_bfloat16*)dx, (__nv_bfloat16*)dz, ws.dzp, ws.cnt, ws.dUp, dU_f32,
+                         (__nv_bfloat16*)dU, (__nv_bfloat16*)(sw ? dsw : nullptr), sp, (int)T, (int)D, R, Rk, residual, tma4);
   if (e != cudaSuccess) {
     cudaGetLastError();
     return cuda_status(e, "cudaLaunchKernelEx(lr_bwd_tc_kernel)");

@@ -66,6 +66,22 @@ int make_btd_map(CUtensorMap* map, const void* base, int64_t B, int64_t T, int64
   return DYNCONV_OK;
 }
 
+int make_btd4_map(CUtensorMap* map, const void* base, int64_t B, int64_t T, int64_t D, int box_t) {
+  EncodeTiledFn fn = encode_fn();
+  if (!fn) return set_error(DYNCONV_ERR_CUDA, "cuTensorMapEncodeTiled unavailable");
+  if (D % 64 != 0) return set_error(DYNCONV_ERR_SHAPE, "4-D channel-group map needs D %% 64 == 0");
+  if (int s = ensure_context()) return s;
+  cuuint64_t dims[4] = {64, (cuuint64_t)T, (cuuint64_t)(D / 64), (cuuint64_t)B};
+  cuuint64_t strides[3] = {(cuuint64_t)D * 2, 128, (cuuint64_t)T * D * 2};
+  cuuint32_t box[4] = {64, (cuuint32_t)box_t, 2, 1};
+  cuuint32_t estr[4] = {1, 1, 1, 1};
+  CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 4, const_cast<void*>(base), dims, strides, box, estr,
+                  CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                  CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return set_error(DYNCONV_ERR_CUDA, "cuTensorMapEncodeTiled(4-D) failed (%d)", (int)r);
+  return DYNCONV_OK;
+}
+
 int make_zpack_map(CUtensorMap* map, const void* base, int64_t B, int64_t T, int rkp, int rows) {
   EncodeTiledFn fn = encode_fn();
   if (!fn) return set_error(DYNCONV_ERR_CUDA, "cuTensorMapEncodeTiled unavailable");

@@ -54,6 +54,12 @@ EncodeTiledFn encode_fn();
 int make_btd_map(CUtensorMap* map, const void* base, int64_t B, int64_t T, int64_t D, int box_d, int box_t,
                  bool swizzle128 = false);
 
+// 4-D bf16 map viewing a [B][T][D] tensor as [B][D/64][T][64] (D % 64 == 0):
+// dims (64, T, D/64, B), box (64, box_t, 2, 1), 128-byte swizzle.  One load then
+// brings 128 channels x box_t steps as two 64-channel swizzle atoms, box_t * 128
+// bytes apart -- the layout two 3-D loads of 64 channels would produce.
+int make_btd4_map(CUtensorMap* map, const void* base, int64_t B, int64_t T, int64_t D, int box_t);
+
 // 4-D bf16 map over z_pack [RKP/8][B][T][8]: dims (8, T, B, RKP/8), box (8, rows, 1, RKP/8).
 // The box lands as [RKP/8][rows][8] (16-byte rows, 8-rank chunks rows*16 bytes apart);
 // rows past T read as zero.
