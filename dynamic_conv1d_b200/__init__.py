@@ -4,7 +4,14 @@
 
 Both ops are ``torch.autograd.Function``s over libdynconv.so, a C-ABI library of
 hand-written sm_100a CUDA kernels (see ``include/dynconv.h``).
+
+Calls never synchronise.  The tensor-core kernels bound every device-side wait
+(1.5 s); a wait that gives up makes its kernel return early and sets a device
+error word, which ``check_device(t)`` reads (raising ``DynconvError`` with status
+DYNCONV_ERR_TIMEOUT).  Call it once per training step (or set DYNCONV_SYNC_CHECK=1
+/ ``set_sync_checks(True)`` to check after every call while debugging).
 """
+from ._lib import DynconvError, check_device, set_sync_checks
 from .headwise import headwise_dynamic_convolution
 from .lowrank import lowrank_dynamic_convolution
 from .modules import LowRankDynamicShortConvolution, QKVLowRankDynamicShortConvolution
@@ -20,4 +27,7 @@ __all__ = [
     "lowrank_dynamic_convolution_sp",
     "headwise_dynamic_convolution_sp",
     "shard_rows",
+    "check_device",
+    "set_sync_checks",
+    "DynconvError",
 ]

@@ -41,6 +41,7 @@ _SIGNATURES = {
     "dynconv_lr_bwd": (_c_int, [_c_vp] * 10 + [_c_vp, _c_size] + [_c_i64] * 5 + [_c_int, _c_int, _c_vp]),
     "dynconv_cast_f32": (_c_int, [_c_vp, _c_vp, _c_i64, _c_int, _c_vp]),
     "dynconv_umma_selftest": (_c_int, [_c_vp, _c_vp, _c_vp] + [_c_int] * 11 + [_c_vp]),
+    "dynconv_wait_selftest": (_c_int, [ctypes.c_uint64, _c_vp, _c_vp]),
 }
 
 EXPORTED_SYMBOLS = tuple(_SIGNATURES)
@@ -118,3 +119,22 @@ def stream_of(t: torch.Tensor):
 def check_device(t: torch.Tensor) -> None:
     """Synchronise the current stream and raise if a device-side bounded wait gave up."""
     check(load().dynconv_check_device(stream_of(t)))
+
+
+_sync_checks = os.environ.get("DYNCONV_SYNC_CHECK", "0") not in ("", "0")
+
+
+def set_sync_checks(enabled: bool) -> None:
+    """Debug mode (also DYNCONV_SYNC_CHECK=1 in the environment): every forward and
+    backward call synchronises its stream and raises DynconvError(DYNCONV_ERR_TIMEOUT)
+    at the call whose kernel gave up a bounded wait.  Off by default: the normal path
+    never synchronises, and a timed-out kernel is reported by the next check_device()."""
+    global _sync_checks
+    _sync_checks = bool(enabled)
+
+
+def after_call(t: torch.Tensor) -> None:
+    """Called by the ops after their launches; checks the device only in debug mode
+    (and never while the stream is being captured into a CUDA graph)."""
+    if _sync_checks and not torch.cuda.is_current_stream_capturing():
+        check_device(t)

@@ -92,6 +92,7 @@ int hw_tma_fwd_launch(const void* x, const void* w, const void* sw, void* y, int
 int hw_tma_bwd_launch(const void* x, const void* w, const void* sw, const void* dy, void* dx, void* dw, float* part,
                       int64_t B, int64_t T, int64_t D, int64_t H, int W, int log2hs, int residual, cudaStream_t st);
 unsigned int selftest_error_word();
+int wait_selftest_launch(uint64_t limit_ns, int* out, cudaStream_t st);
 
 // kernels (other translation units)
 int hw_partial_rows(int64_t B, int64_t T, int64_t D, int dtype);
@@ -176,11 +177,15 @@ int dynconv_check_device(void* stream) {
   cudaStream_t st = (cudaStream_t)stream;
   cudaError_t e = cudaStreamSynchronize(st);
   if (e != cudaSuccess) return cuda_status(e, "cudaStreamSynchronize");
+  // every word is read (and so cleared) before the first non-zero one is reported
   const unsigned int words[4] = {lr_tc_error_word(), lr_bwd_error_word(), selftest_error_word(), hw_tma_error_word()};
-  for (unsigned int v : words) {
+  static const char* const kFile[4] = {"lowrank forward", "lowrank backward", "self-test", "headwise"};
+  for (unsigned int v : words)
     if (v == 0xFFFFFFFFu) return set_error(DYNCONV_ERR_CUDA, "could not read the device error word");
-    if (v != 0) return set_error(DYNCONV_ERR_TIMEOUT, "a device-side bounded wait gave up (site %u)", v);
-  }
+  for (int i = 0; i < 4; ++i)
+    if (words[i] != 0)
+      return set_error(DYNCONV_ERR_TIMEOUT, "a device-side bounded wait gave up (%s kernel, site %u)", kFile[i],
+                       words[i]);
   return DYNCONV_OK;
 }
 
@@ -355,6 +360,13 @@ int dynconv_umma_selftest(const void* A, const void* B, float* D, int M, int N, 
   if (!A || !B || !D) return set_error(DYNCONV_ERR_ARGUMENT, "selftest: null pointer");
   return umma_selftest_launch(A, B, D, M, N, K, Nb, a_major, a_sbo, a_lbo, b_major, b_sbo, b_lbo, b_row_offset,
                               (cudaStream_t)stream);
+}
+
+int dynconv_wait_selftest(uint64_t limit_ns, int* out, void* stream) {
+  if (limit_ns == 0 || limit_ns > 100000000ull)
+    return set_error(DYNCONV_ERR_ARGUMENT, "wait_selftest: limit %llu ns outside 1 ns .. 100 ms",
+                     (unsigned long long)limit_ns);
+  return wait_selftest_launch(limit_ns, out, (cudaStream_t)stream);
 }
 
 }  // extern "C"

@@ -272,13 +272,14 @@ constexpr uint32_t kWaitSuspendNs = 1000000u;       // longest single suspension
 // Slow path of mbar_wait, kept out of line so that the many wait sites of a
 // warp-specialised kernel stay small in the instruction cache.
 static __device__ __noinline__ bool mbar_wait_slow(uint64_t* bar, uint32_t parity, unsigned int site,
-                                            volatile int* abort_flag) {
+                                                   volatile int* abort_flag, uint64_t limit_ns = kWaitLimitNs) {
   if (*abort_flag) return false;
   const uint64_t t0 = globaltimer_ns();
+  const uint32_t suspend = limit_ns < kWaitSuspendNs ? (uint32_t)limit_ns : kWaitSuspendNs;
   for (;;) {
-    if (mbar_try_wait_suspend(bar, parity, kWaitSuspendNs)) return true;
+    if (mbar_try_wait_suspend(bar, parity, suspend)) return true;
     if (*abort_flag) return false;
-    if (globaltimer_ns() - t0 > kWaitLimitNs) break;
+    if (globaltimer_ns() - t0 > limit_ns) break;
   }
   atomicCAS(&g_device_error, 0u, site);
   *abort_flag = 1;

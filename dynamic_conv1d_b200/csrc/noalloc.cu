@@ -34,7 +34,9 @@ void* g_scratch_ptr[kMaxDevices] = {};
 
 // Address of this device's scratch array.  The first call per device does the
 // set-up (it also makes the runtime load this module on that device); later
-// calls only read the cached pointer.
+// calls only read the cached pointer.  Keyed by device ordinal: the library runs
+// in each device's primary context only (ensure_context binds it), so one
+// module instance -- one scratch address -- exists per device.
 int scratch_for_current_device(void** out) {
   int dev = -1;
   cudaError_t e = cudaGetDevice(&dev);

@@ -149,4 +149,29 @@ int umma_selftest_launch(const void* A, const void* B, float* D, int M, int N, i
   return DYNCONV_OK;
 }
 
+// A wait that nobody ends: one CTA waits on an mbarrier that no thread arrives on,
+// through the same bounded slow path the kernels use, with a short limit.  The
+// wait gives up, records its site in this file's device error word, raises the
+// CTA's abort flag and returns; the kernel then exits normally.  Exercises the
+// timeout path end to end (dynconv_check_device reports DYNCONV_ERR_TIMEOUT).
+__global__ void __launch_bounds__(32) wait_selftest_kernel(uint64_t limit_ns, int* out) {
+  __shared__ uint64_t bar;
+  __shared__ int abort_flag;
+  if (threadIdx.x == 0) {
+    mbar_init(&bar, 1);
+    abort_flag = 0;
+    fence_barrier_init();
+  }
+  __syncwarp();
+  bool ok = mbar_try_wait(&bar, 0);
+  if (!ok) ok = mbar_wait_slow(&bar, 0, kErrWaitTail, &abort_flag, limit_ns);
+  if (threadIdx.x == 0 && out) out[0] = ok ? 1 : 0;
+}
+
+int wait_selftest_launch(uint64_t limit_ns, int* out, cudaStream_t st) {
+  wait_selftest_kernel<<<1, 32, 0, st>>>(limit_ns, out);
+  DYNCONV_CHECK_LAUNCH("wait_selftest_kernel");
+  return DYNCONV_OK;
+}
+
 }  // namespace dynconv

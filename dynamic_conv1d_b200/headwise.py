@@ -37,6 +37,7 @@ class _HeadwiseDynamicConvolutionFn(torch.autograd.Function):
                 B, T, D, H, W, code, int(bool(residual)), _lib.stream_of(x),
             )
         )
+        _lib.after_call(y)
         ctx.save_for_backward(x, w_k, static_w)
         ctx.weight_dtype = weight.dtype
         ctx.residual = bool(residual)
@@ -78,6 +79,7 @@ class _HeadwiseDynamicConvolutionFn(torch.autograd.Function):
             dsw = torch.empty((W, D), device=x.device, dtype=static_w.dtype)
             _lib.check(lib.dynconv_cast_f32(_lib.ptr(dsw_f32), _lib.ptr(dsw), W * D,
                                             _lib.dtype_code(static_w.dtype), stream))
+        _lib.after_call(dx)
         if ctx.weight_dtype != dw.dtype:
             dw = dw.to(ctx.weight_dtype)
         return dx, dw, dsw, None

@@ -50,6 +50,7 @@ class _LowrankDynamicConvolutionFn(torch.autograd.Function):
                 B, T, D, R, W, code, int(bool(residual)), _lib.stream_of(x),
             )
         )
+        _lib.after_call(y)
         ctx.save_for_backward(x, z_k, U_k, sw_k)
         ctx.dtypes = (z.dtype, U.dtype, None if static_w is None else static_w.dtype)
         ctx.residual = bool(residual)
@@ -96,6 +97,7 @@ class _LowrankDynamicConvolutionFn(torch.autograd.Function):
             dU = g[:R]
             if has_static:
                 dsw = g[R].view(W, D)
+        _lib.after_call(dx)
         z_dt, U_dt, sw_dt = ctx.dtypes
         if dz.dtype != z_dt:
             dz = dz.to(z_dt)

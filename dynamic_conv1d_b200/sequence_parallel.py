@@ -44,6 +44,18 @@ def _exchange(send: torch.Tensor | None, send_to: int | None, recv_shape, recv_f
     return recv
 
 
+def _check_lengths(T: int, h: int, device, group) -> None:
+    """Every rank must hold at least h = W-1 steps.  The shortest slice is agreed on
+    by a MIN all-reduce before any point-to-point exchange, so that all ranks raise
+    together instead of some of them waiting on a halo that never comes."""
+    t = torch.tensor([T], dtype=torch.int64, device=device)
+    dist.all_reduce(t, op=dist.ReduceOp.MIN, group=group)
+    t_min = int(t.item())
+    if t_min < h:
+        raise ValueError(f"sequence parallel: each rank needs at least W-1={h} steps; "
+                         f"the shortest slice holds {t_min} (this rank {T})")
+
+
 class _HaloPrepend(torch.autograd.Function):
     """[B, T, D] -> [B, h + T, D]: the previous rank's last h rows, then the local rows."""
 
@@ -52,8 +64,7 @@ class _HaloPrepend(torch.autograd.Function):
         world = dist.get_world_size(group)
         rank = dist.get_rank(group)
         B, T = x.shape[0], x.shape[1]
-        if T < h:
-            raise ValueError(f"sequence parallel: each rank needs at least W-1={h} steps, this one holds {T}")
+        _check_lengths(T, h, x.device, group)
         send = x[:, T - h:].contiguous()
         halo = _exchange(send, rank + 1 if rank + 1 < world else None, (B, h) + tuple(x.shape[2:]),
                          rank - 1 if rank > 0 else None, x, group)

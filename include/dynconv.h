@@ -15,6 +15,16 @@
  *     the last failing call on the calling thread is dynconv_last_error().
  *   - Shapes: x,y,dx,dy [B,T,D]; headwise weight [B,T,H,W]; lowrank z [B,T,R],
  *     U [R, W*D] (viewed as [R][W][D]); static_w [W,D].  W in 1..8.
+ *   - Contexts: the library works in the primary context of the current device
+ *     (the one the CUDA runtime and PyTorch use).  On a thread with no current
+ *     context it makes that primary context current.  Contexts created with
+ *     cuCtxCreate are not supported: device pointers, streams and the per-device
+ *     state below (the noalloc scratch address, cached SM counts) all belong to
+ *     the primary context.
+ *   - Errors on the device: the tensor-core kernels bound every wait (1.5 s).  A
+ *     wait that gives up makes its kernel return early and sets a device error
+ *     word; the call itself has already returned DYNCONV_OK, so check once per
+ *     step with dynconv_check_device (it synchronises the stream).
  */
 #ifndef DYNCONV_H_
 #define DYNCONV_H_
@@ -123,6 +133,8 @@ int dynconv_lr_fwd(const void* x, const void* z, const void* U, const void* stat
  *   - The first call on each device (with that device current) does a one-time
  *     set-up: it looks up the scratch address, which also loads the library's
  *     module on that device.  Make that first call before any stream capture.
+ *     The address is cached per device ordinal, for the device's primary context
+ *     (the only kind of context the library supports).
  *   - Sizes whose workspace (dynconv_lr_fwd_workspace_bytes) exceeds the scratch
  *     are rejected with DYNCONV_ERR_WORKSPACE; use dynconv_lr_fwd for those.
  *   - All calls on one device share the one scratch array: two calls that can
@@ -170,6 +182,14 @@ int dynconv_umma_selftest(const void* A, const void* B, float* D,
                           int a_major, int a_sbo, int a_lbo,
                           int b_major, int b_sbo, int b_lbo, int b_row_offset,
                           void* stream);
+
+/* Test hook for the fault-containment path (no reference counterpart): launches one
+ * CTA that waits on an mbarrier no thread ever arrives on, through the kernels'
+ * bounded-wait code, with a limit of limit_ns (1 ns .. 100 ms).  The wait gives up,
+ * sets the device error word and the kernel returns; a following
+ * dynconv_check_device() reports DYNCONV_ERR_TIMEOUT once and clears the word.
+ * out (device int, may be NULL) receives 0 when the wait gave up. */
+int dynconv_wait_selftest(uint64_t limit_ns, int* out, void* stream);
 
 #if defined(__GNUC__)
 #pragma GCC visibility pop

@@ -132,38 +132,38 @@ def test_entry_point_from_a_fresh_thread(cuda_device):
 SP_CHILD = textwrap.dedent(
     """
     import sys, datetime
+    import numpy as np
     import torch, torch.distributed as dist
     sys.path.insert(0, {root!r})
-    from dynamic_conv1d_b200 import (headwise_dynamic_convolution, headwise_dynamic_convolution_sp,
-                                     lowrank_dynamic_convolution, lowrank_dynamic_convolution_sp)
+    import oracle
+    from dynamic_conv1d_b200 import headwise_dynamic_convolution_sp, lowrank_dynamic_convolution_sp
     dist.init_process_group("nccl", init_method="tcp://127.0.0.1:{port}", rank=0, world_size=1,
                             timeout=datetime.timedelta(seconds=60), device_id=torch.device("cuda", 0))
     dev = torch.device("cuda", 0)
     g = torch.Generator().manual_seed(6)
     bf = torch.bfloat16
     def rnd(*s, scale=1.0):
-        return (torch.randn(*s, generator=g) * scale).to(bf).to(dev)
-    def rel(a, b):
-        return ((a.float() - b.float()).norm() / b.float().norm().clamp_min(1e-30)).item()
+        return (torch.randn(*s, generator=g) * scale).to(bf)
+    def rel(a, ref):
+        a = a.detach().float().cpu().numpy().astype(np.float64)
+        return np.linalg.norm(a - ref) / max(np.linalg.norm(ref), 1e-30)
     B, T, D, W = 2, 200, 256, 4
     x, dy = rnd(B, T, D), rnd(B, T, D)
     cases = {{
-        "lowrank": (lowrank_dynamic_convolution, lowrank_dynamic_convolution_sp,
+        "lowrank": (lowrank_dynamic_convolution_sp, oracle.lowrank_fwd, oracle.lowrank_bwd,
                     [x, rnd(B, T, 15), rnd(15, W * D, scale=0.25), rnd(W, D, scale=0.3)]),
-        "headwise": (headwise_dynamic_convolution, headwise_dynamic_convolution_sp,
+        "headwise": (headwise_dynamic_convolution_sp, oracle.headwise_fwd, oracle.headwise_bwd,
                      [x, rnd(B, T, D // 32, W, scale=0.3), rnd(W, D, scale=0.3)]),
     }}
-    for name, (fn, fn_sp, leaves0) in cases.items():
-        outs = []
-        for f in (fn, fn_sp):
-            leaves = [t.clone().requires_grad_() for t in leaves0]
-            y = f(*leaves, residual=True)
-            y.backward(dy)
-            torch.cuda.synchronize()
-            outs.append([y.detach()] + [l.grad for l in leaves])
-        for i, (a, b) in enumerate(zip(*outs)):
-            assert a.shape == b.shape, (name, i)
-            e = rel(b, a)
+    f = lambda t: t.float().numpy()
+    for name, (fn_sp, ofwd, obwd, cpu) in cases.items():
+        leaves = [t.to(dev).requires_grad_() for t in cpu]
+        y = fn_sp(*leaves, residual=True)
+        y.backward(dy.to(dev))
+        torch.cuda.synchronize()
+        refs = [ofwd(*map(f, cpu), True)] + list(obwd(*map(f, cpu), f(dy), True))
+        for i, (a, ref) in enumerate(zip([y] + [l.grad for l in leaves], refs)):
+            e = rel(a, ref)
             assert e <= (1e-2 if i == 0 else 2e-2), (name, i, e)
         print("ok", name)
     dist.destroy_process_group()
@@ -171,9 +171,9 @@ SP_CHILD = textwrap.dedent(
 )
 
 
-def test_sequence_parallel_one_rank_matches_direct(cuda_device):
-    """Time-sharded wrappers on one NCCL rank: the halo is the zero padding and the
-    results match the direct op within the bf16 tolerances."""
+def test_sequence_parallel_one_rank_matches_oracle(cuda_device):
+    """Time-sharded wrappers on one NCCL rank: the halo is the zero padding; output
+    and all gradients match the CPU oracle (rel-L2 1e-2 for y, 2e-2 for gradients)."""
     code = SP_CHILD.format(root=ROOT, port=_free_port())
     r = subprocess.run([sys.executable, "-c", code], capture_output=True, text=True, timeout=240)
     assert r.returncode == 0, r.stdout[-2000:] + r.stderr[-4000:]
@@ -223,10 +223,11 @@ def test_tensors_on_a_non_current_device():
 SP2_SCRIPT = textwrap.dedent(
     """
     import datetime, os, sys
+    import numpy as np
     import torch, torch.distributed as dist
     sys.path.insert(0, {root!r})
-    from dynamic_conv1d_b200 import (headwise_dynamic_convolution, headwise_dynamic_convolution_sp,
-                                     lowrank_dynamic_convolution, lowrank_dynamic_convolution_sp)
+    import oracle
+    from dynamic_conv1d_b200 import headwise_dynamic_convolution_sp, lowrank_dynamic_convolution_sp
     rank, world = int(os.environ["RANK"]), int(os.environ["WORLD_SIZE"])
     dev = torch.device("cuda", rank)
     torch.cuda.set_device(dev)
@@ -235,33 +236,32 @@ SP2_SCRIPT = textwrap.dedent(
     bf = torch.bfloat16
     def rnd(*s, scale=1.0):
         return (torch.randn(*s, generator=g) * scale).to(bf)
-    def rel(a, b):
-        return ((a.float() - b.float()).norm() / b.float().norm().clamp_min(1e-30)).item()
-    B, T, D, W = 2, 256, 256, 4
+    def rel(a, ref):
+        a = a.detach().float().cpu().numpy().astype(np.float64)
+        return np.linalg.norm(a - ref) / max(np.linalg.norm(ref), 1e-30)
+    B, T, D, W = 2, 300, 256, 4
     x, dy = rnd(B, T, D), rnd(B, T, D)
     cases = {{
-        "lowrank": (lowrank_dynamic_convolution, lowrank_dynamic_convolution_sp,
+        "lowrank": (lowrank_dynamic_convolution_sp, oracle.lowrank_fwd, oracle.lowrank_bwd,
                     [x, rnd(B, T, 15), rnd(15, W * D, scale=0.25), rnd(W, D, scale=0.3)], 2),
-        "headwise": (headwise_dynamic_convolution, headwise_dynamic_convolution_sp,
+        "headwise": (headwise_dynamic_convolution_sp, oracle.headwise_fwd, oracle.headwise_bwd,
                      [x, rnd(B, T, D // 32, W, scale=0.3), rnd(W, D, scale=0.3)], 2),
     }}
     lo, hi = rank * T // world, (rank + 1) * T // world
-    for name, (fn, fn_sp, cpu, n_local) in cases.items():
+    f = lambda t: t.float().numpy()
+    for name, (fn_sp, ofwd, obwd, cpu, n_local) in cases.items():
         # time-sharded: x and the mixing input are split, the shared parameters replicated
         leaves = [t[:, lo:hi].contiguous().to(dev) if i < n_local else t.to(dev) for i, t in enumerate(cpu)]
         leaves = [t.requires_grad_() for t in leaves]
         y = fn_sp(*leaves, residual=True)
         y.backward(dy[:, lo:hi].contiguous().to(dev))
         torch.cuda.synchronize()
-        # full sequence on this GPU
-        full = [t.to(dev).requires_grad_() for t in cpu]
-        yf = fn(*full, residual=True)
-        yf.backward(dy.to(dev))
-        torch.cuda.synchronize()
-        pairs = [(y, yf[:, lo:hi])] + [(l.grad, f.grad[:, lo:hi]) for l, f in zip(leaves[:n_local], full[:n_local])] \\
-            + [(l.grad, f.grad) for l, f in zip(leaves[n_local:], full[n_local:])]
-        for i, (a, b) in enumerate(pairs):
-            e = rel(a, b)
+        # the full sequence on the CPU oracle; this rank's slice of it
+        ry = ofwd(*map(f, cpu), True)
+        rg = obwd(*map(f, cpu), f(dy), True)
+        refs = [ry[:, lo:hi]] + [r[:, lo:hi] for r in rg[:n_local]] + list(rg[n_local:])
+        for i, (a, ref) in enumerate(zip([y] + [l.grad for l in leaves], refs)):
+            e = rel(a, ref)
             assert e <= (1e-2 if i == 0 else 2e-2), (name, rank, i, e)
         print("ok", name, rank, flush=True)
     dist.barrier()
@@ -271,8 +271,9 @@ SP2_SCRIPT = textwrap.dedent(
 
 
 def test_sequence_parallel_two_gpus(tmp_path):
-    """Time axis split over two GPUs (NCCL point-to-point halo exchange): each rank's
-    output and gradients match the full-sequence computation (needs two GPUs)."""
+    """Time axis split over two GPUs (NCCL point-to-point halo exchange, shared
+    gradients all-reduced): each rank's output and gradients match its slice of the
+    full-sequence CPU oracle (needs two GPUs)."""
     import torch
 
     if not torch.cuda.is_available() or torch.cuda.device_count() < 2:

@@ -1,5 +1,8 @@
-"""GPU parity at the BASELINE.json benchmark shapes (configs[1..3]) against the CPU
+"""GPU parity at the BASELINE.json benchmark shapes (configs[1..4]) against the CPU
 oracle on the same bf16 values: relative L2 <= 1e-2 (y) and <= 2e-2 (gradients).
+configs[4] (the data-parallel scale-out, 8 rows of T=8192, D=4096 per GPU at 8
+GPUs) is checked on one full row: the same tiles, rank 32 and channel blocks per
+tile as every rank runs, at a size the numpy oracle finishes in seconds.
 
 At these sizes every CTA of the persistent kernels walks many tiles, the dz
 reduction crosses all 16 channel-block CTAs of a tile, and the dU / dstatic_w
@@ -20,6 +23,7 @@ CONFIGS = {
     "cfg2_headwise_hs32": dict(kind="headwise", B=4, T=4096, D=2048, H=64, W=4),
     "cfg3_headwise_hs1": dict(kind="headwise", B=4, T=4096, D=2048, H=2048, W=4),
     "cfg4_lowrank_r15_static": dict(kind="lowrank", B=4, T=4096, D=2048, R=15, W=4),
+    "cfg5_lowrank_r31_static_row": dict(kind="lowrank", B=1, T=8192, D=4096, R=31, W=4),
 }
 
 

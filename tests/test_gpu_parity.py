@@ -169,6 +169,11 @@ EDGE = [
     ("lowrank", 1, 8192, 512, 31, 4, True, True),   # R_kernel = 32
     ("lowrank", 3, 3000, 384, 15, 3, True, True),   # W = 3, ragged T
     ("headwise", 2, 2048, 1024, 32, 4, True, True),
+    # R_kernel = 64 and W = 8 over many tiles per CTA
+    ("lowrank", 1, 4096, 512, 63, 4, True, True),
+    ("lowrank", 2, 1500, 256, 64, 2, False, True),
+    ("lowrank", 2, 2048, 512, 15, 8, True, True),
+    ("headwise", 2, 2048, 512, 16, 8, True, True),
 ]
 
 

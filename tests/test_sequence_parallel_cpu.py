@@ -140,3 +140,43 @@ def test_sequence_parallel_headwise_matches_full_sequence():
     y = ref_headwise(*leaves, residual=True)
     y.backward(dy)
     _check(res, leaves, y)
+
+
+def _short_worker(rank, world, port, q):
+    try:
+        from dynamic_conv1d_b200.sequence_parallel import sequence_parallel
+
+        os.environ["MASTER_ADDR"] = "127.0.0.1"
+        os.environ["MASTER_PORT"] = str(port)
+        dist.init_process_group("gloo", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=30))
+        x, z, U, sw, _ = _inputs(T=12, W=4)
+        # rank 1 holds only 2 steps (< W-1 = 3); rank 0 holds 10
+        lo, hi = (0, 10) if rank == 0 else (10, 12)
+        try:
+            sequence_parallel(ref_lowrank, x[:, lo:hi], z[:, lo:hi], U, sw, residual=True, W=4)
+            q.put((rank, "no error"))
+        except ValueError as e:
+            q.put((rank, "raised", str(e)))
+        dist.destroy_process_group()
+    except Exception:
+        import traceback
+
+        q.put((rank, "error", traceback.format_exc()))
+
+
+def test_sequence_parallel_short_slice_raises_on_every_rank():
+    """A slice shorter than W-1 on one rank makes every rank raise before the halo
+    exchange (no rank is left waiting on a halo that is never sent)."""
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        port = s.getsockname()[1]
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    procs = [ctx.Process(target=_short_worker, args=(r, 2, port, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    res = sorted(q.get(timeout=120) for _ in range(2))
+    for p in procs:
+        p.join(timeout=60)
+    assert [r[1] for r in res] == ["raised", "raised"], res
+    assert "shortest slice holds 2" in res[0][2]
