@@ -335,6 +335,16 @@ def device_inputs(wl: dict, dev, seed: int):
     return [x, wgt, sw], dy
 
 
+def _backward(y, dy):
+    """y.backward(dy), or one backward over several outputs (a tuple of y and of dy)."""
+    import torch
+
+    if isinstance(y, (tuple, list)):
+        torch.autograd.backward(list(y), list(dy))
+    else:
+        y.backward(dy)
+
+
 class DeviceStep:
     """One fwd+bwd step of `fn` on resident inputs, captured in a CUDA graph (eager if
     capture fails), timed with CUDA events per step with an L2 flush before each."""
@@ -364,8 +374,7 @@ class DeviceStep:
                 for l in leaves:
                     l.grad = None
                 with torch.cuda.graph(graph), dp_ctx():
-                    y_static = fn(*leaves, residual=self.res)
-                    y_static.backward(dy)
+                    _backward(fn(*leaves, residual=self.res), dy)
                 torch.cuda.synchronize()
                 self.graph = graph
             except Exception as e:  # pragma: no cover - reported in the JSON line
@@ -375,7 +384,7 @@ class DeviceStep:
         for l in self.leaves:
             l.grad = None
         y = self.fn(*self.leaves, residual=self.res)
-        y.backward(self.dy)
+        _backward(y, self.dy)
         return y
 
     def run_one(self):
@@ -497,6 +506,69 @@ def sub_workload(args, name: str, wl: dict, dev, world: int, local: int, rank: i
     return out
 
 
+def qkv_workload(args, dev, world: int, local: int, rank: int, flush) -> dict:
+    """The query, key and value convolutions of one attention layer on configs[3]'s
+    shapes (README.md:86-105: three LowRankDynamicShortConvolution modules): the
+    grouped op -- one forward and one backward launch over the fused [B, T, 3D]
+    activations, one stacked dU all-reduce under DP -- against three separate
+    calls on already-contiguous per-group tensors, both device-timed the same way."""
+    import torch
+
+    from dynamic_conv1d_b200 import lowrank_dynamic_convolution, lowrank_dynamic_convolution_grouped
+
+    wl = dict(WORKLOADS["lowrank"])
+    G, B, T, D, R, W = 3, wl["B"], wl["T"], wl["D"], wl["R"], wl["W"]
+    bf = torch.bfloat16
+    g = torch.Generator(device=dev).manual_seed(300 + rank)
+    gs = torch.Generator(device=dev).manual_seed(9)
+    x = torch.randn(B, T, G * D, device=dev, generator=g).to(bf)
+    dy = torch.randn(B, T, G * D, device=dev, generator=g).to(bf)
+    z = torch.randn(B, T, G * R, device=dev, generator=g).to(bf)
+    U = (torch.randn(G, R, W * D, device=dev, generator=gs) / np.sqrt(R)).to(bf)
+    sw = (torch.rand(G, W, D, device=dev, generator=gs) - 0.5).to(bf)
+    leaves = [t.clone().requires_grad_() for t in (x, z, U, sw)]
+    dp_ctx = _dp_ctx_factory(world)
+    steps = max(5, min(args.steps, 10))
+    ds = DeviceStep(args, wl, leaves, dy, lowrank_dynamic_convolution_grouped, dev, world, dp_ctx, flush)
+    m = ds.measure(steps, local)
+    ds.release()
+
+    sep = []
+    for i in range(G):
+        sep += [x[..., i * D:(i + 1) * D].contiguous(), z[..., i * R:(i + 1) * R].contiguous(), U[i].contiguous(),
+                sw[i].contiguous()]
+    sep = [t.requires_grad_() for t in sep]
+    dy3 = tuple(dy[..., i * D:(i + 1) * D].contiguous() for i in range(G))
+
+    def three(*ls, residual):
+        return tuple(lowrank_dynamic_convolution(*ls[4 * i:4 * i + 4], residual=residual) for i in range(G))
+
+    ds3 = DeviceStep(args, wl, sep, dy3, three, dev, world, dp_ctx, flush)
+    m3 = ds3.measure(steps, local)
+    ds3.release()
+    fwd_b, bwd_b = algorithmic_bytes(wl)
+    peak = _peaks()[0]
+    ms, ms3 = m["total_ms"] / steps, m3["total_ms"] / steps
+    out = {
+        "value": world * B * T * steps / (m["total_ms"] / 1e3) / 1e6,
+        "unit": "Mtokens/s (three convolutions per token)",
+        "ms_per_step": ms,
+        "steps": steps,
+        "scaling": "weak",
+        "config": {**wl, "G": G, "layout": "x, y [B, T, 3D] (fused QKV projection output); z [B, T, 3R]",
+                   "global_batch": B * world, "parallelism": f"dp{world}"},
+        "hbm_roofline_frac_step": G * (fwd_b + bwd_b) / (ms / 1e3) / (peak * 1e9),
+        "gpu_launches": m["launches"],
+        "separate_calls": {"ms_per_step": ms3, "gpu_launches": m3["launches"],
+                           "hbm_roofline_frac_step": G * (fwd_b + bwd_b) / (ms3 / 1e3) / (peak * 1e9)},
+        "speedup_vs_separate": ms3 / ms,
+        "clocks": m["clocks"],
+    }
+    del leaves, sep, ds, ds3
+    torch.cuda.empty_cache()
+    return out
+
+
 def run_ours(args, wl: dict) -> None:
     import torch
     import torch.distributed as dist
@@ -565,6 +637,7 @@ def run_ours(args, wl: dict) -> None:
         cfg5 = dict(WORKLOADS["lowrank_dp"])
         cfg5["B"] = max(1, 64 // world)
         subs["lowrank_dp_cfg5"] = sub_workload(args, "lowrank_dp", cfg5, dev, world, local, rank, flush, "strong")
+        subs["lowrank_qkv_cfg4"] = qkv_workload(args, dev, world, local, rank, flush)
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:

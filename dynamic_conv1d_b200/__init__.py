@@ -13,7 +13,7 @@ DYNCONV_ERR_TIMEOUT).  Call it once per training step (or set DYNCONV_SYNC_CHECK
 """
 from ._lib import DynconvError, check_device, set_sync_checks
 from .headwise import headwise_dynamic_convolution
-from .lowrank import lowrank_dynamic_convolution
+from .lowrank import lowrank_dynamic_convolution, lowrank_dynamic_convolution_grouped
 from .modules import LowRankDynamicShortConvolution, QKVLowRankDynamicShortConvolution
 from .parallel import data_parallel, shard_rows
 from .sequence_parallel import headwise_dynamic_convolution_sp, lowrank_dynamic_convolution_sp
@@ -21,6 +21,7 @@ from .sequence_parallel import headwise_dynamic_convolution_sp, lowrank_dynamic_
 __all__ = [
     "headwise_dynamic_convolution",
     "lowrank_dynamic_convolution",
+    "lowrank_dynamic_convolution_grouped",
     "LowRankDynamicShortConvolution",
     "QKVLowRankDynamicShortConvolution",
     "data_parallel",

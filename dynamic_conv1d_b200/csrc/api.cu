@@ -110,20 +110,21 @@ int lr_bwd_simple_launch(const void* x, const void* z, const void* U, const void
                          void* dz, float* part, int64_t B, int64_t T, int64_t D, int R, int Rk, int W, int dtype,
                          int residual, cudaStream_t st);
 int umma_selftest_launch(const void* A, const void* B, float* D, int M, int N, int K, int Nb, int a_major, int a_sbo,
-                         int a_lbo, int b_major, int b_sbo, int b_lbo, int b_off, cudaStream_t st);
-bool lr_tc_supported(int64_t D, int Rk, int W, int dtype, const void* const* ptrs, int nptrs);
-bool lr_tc_bwd_supported(int64_t D, int Rk, int W, int dtype, const void* const* ptrs, int nptrs);
-size_t lr_tc_bwd_workspace(int64_t B, int64_t T, int64_t D, int Rk, int W);
-size_t lr_tc_fwd_workspace(int64_t B, int64_t T, int Rk);
+                         int a_lbo, int b_major, int b_sbo, int b_lbo, int b_off, int a_off, cudaStream_t st);
+bool lr_tc_supported(int64_t D, int Rk, int W, int dtype, const void* const* ptrs, int nptrs, int G);
+bool lr_tc_bwd_supported(int64_t D, int Rk, int W, int dtype, const void* const* ptrs, int nptrs, int G);
+size_t lr_tc_bwd_workspace(int64_t B, int64_t T, int64_t D, int Rk, int W, int G);
+size_t lr_tc_fwd_workspace(int64_t B, int64_t T, int Rk, int G);
 int lr_tc_fwd_launch(const void* x, const void* z, const void* U, const void* sw, void* y, void* ws, size_t ws_bytes,
-                     int64_t B, int64_t T, int64_t D, int R, int Rk, int W, int residual, cudaStream_t st);
+                     int64_t B, int64_t T, int64_t D, int G, int R, int Rk, int W, int residual, cudaStream_t st);
 int lr_tc_bwd_launch(const void* x, const void* z, const void* U, const void* sw, const void* dy, void* dx, void* dz,
                      float* dU_f32, void* dU, void* dsw, void* ws, size_t ws_bytes, int64_t B, int64_t T, int64_t D,
-                     int R, int Rk, int W, int residual, cudaStream_t st);
+                     int G, int R, int Rk, int W, int residual, cudaStream_t st);
 
 namespace {
 
 constexpr size_t kAlign = 256;
+constexpr int kMaxGroups = 16;
 size_t align_up(size_t v) { return (v + kAlign - 1) / kAlign * kAlign; }
 
 int check_dtype(int dtype) {
@@ -271,80 +272,136 @@ static int lr_checks(int64_t B, int64_t T, int64_t D, int64_t R, int64_t W, int 
   return DYNCONV_OK;
 }
 
-size_t dynconv_lr_fwd_workspace_bytes(int64_t B, int64_t T, int64_t D, int64_t R, int64_t W, int dtype,
-                                      int has_static) {
-  const int Rk = (int)R + (has_static ? 1 : 0);
-  if (B * T == 0 || !lr_tc_supported(D, Rk, (int)W, dtype, nullptr, 0)) return 0;
-  return lr_tc_fwd_workspace(B, T, Rk);
+static int check_groups(int64_t G) {
+  if (G < 1 || G > kMaxGroups)
+    return set_error(DYNCONV_ERR_SHAPE, "G=%lld channel groups outside 1..%d", (long long)G, kMaxGroups);
+  return DYNCONV_OK;
 }
 
-int dynconv_lr_fwd(const void* x, const void* z, const void* U, const void* static_w, void* y, void* workspace,
-                   size_t workspace_bytes, int64_t B, int64_t T, int64_t D, int64_t R, int64_t W, int dtype,
-                   int residual, void* stream) {
+size_t dynconv_lr_fwd_grouped_workspace_bytes(int64_t B, int64_t T, int64_t D, int64_t R, int64_t W, int64_t G,
+                                              int dtype, int has_static) {
+  const int Rk = (int)R + (has_static ? 1 : 0);
+  if (B * T == 0 || G < 1 || G > kMaxGroups || !lr_tc_supported(D, Rk, (int)W, dtype, nullptr, 0, (int)G)) return 0;
+  return lr_tc_fwd_workspace(B, T, Rk, (int)G);
+}
+
+size_t dynconv_lr_fwd_workspace_bytes(int64_t B, int64_t T, int64_t D, int64_t R, int64_t W, int dtype,
+                                      int has_static) {
+  return dynconv_lr_fwd_grouped_workspace_bytes(B, T, D, R, W, 1, dtype, has_static);
+}
+
+int dynconv_lr_fwd_grouped(const void* x, const void* z, const void* U, const void* static_w, void* y,
+                           void* workspace, size_t workspace_bytes, int64_t B, int64_t T, int64_t D, int64_t R,
+                           int64_t W, int64_t G, int dtype, int residual, void* stream) {
   int s;
   if ((s = lr_checks(B, T, D, R, W, dtype))) return s;
+  if ((s = check_groups(G))) return s;
   const int Rk = (int)R + (static_w ? 1 : 0);
   if (Rk > 64) return set_error(DYNCONV_ERR_UNSUPPORTED, "R_kernel=%d > 64", Rk);
   if (B * T == 0) return DYNCONV_OK;
   if (!x || !z || !U || !y) return set_error(DYNCONV_ERR_ARGUMENT, "lr_fwd: null tensor");
   cudaStream_t st = (cudaStream_t)stream;
   const void* ptrs[] = {x, z, U, static_w, y, workspace};
-  if (lr_tc_supported(D, Rk, (int)W, dtype, ptrs, 6)) {
-    const size_t need = lr_tc_fwd_workspace(B, T, Rk);
+  if (lr_tc_supported(D, Rk, (int)W, dtype, ptrs, 6, (int)G)) {
+    const size_t need = lr_tc_fwd_workspace(B, T, Rk, (int)G);
     if (!workspace || workspace_bytes < need)
       return set_error(DYNCONV_ERR_WORKSPACE, "lr_fwd: workspace %zu < %zu bytes", workspace_bytes, need);
-    return lr_tc_fwd_launch(x, z, U, static_w, y, workspace, workspace_bytes, B, T, D, (int)R, Rk, (int)W, residual,
-                            st);
+    return lr_tc_fwd_launch(x, z, U, static_w, y, workspace, workspace_bytes, B, T, D, (int)G, (int)R, Rk, (int)W,
+                            residual, st);
   }
+  if (G > 1)
+    return set_error(DYNCONV_ERR_UNSUPPORTED,
+                     "lr_fwd_grouped: G=%lld groups need the tensor-core path (bf16, W <= 4, R_kernel <= 64, "
+                     "D %% 128 == 0, 16-byte aligned tensors); call dynconv_lr_fwd per group",
+                     (long long)G);
   return lr_fwd_simple_launch(x, z, U, static_w, y, B, T, D, (int)R, Rk, (int)W, dtype, residual, st);
+}
+
+int dynconv_lr_fwd(const void* x, const void* z, const void* U, const void* static_w, void* y, void* workspace,
+                   size_t workspace_bytes, int64_t B, int64_t T, int64_t D, int64_t R, int64_t W, int dtype,
+                   int residual, void* stream) {
+  return dynconv_lr_fwd_grouped(x, z, U, static_w, y, workspace, workspace_bytes, B, T, D, R, W, 1, dtype, residual,
+                                stream);
+}
+
+size_t dynconv_lr_bwd_grouped_workspace_bytes(int64_t B, int64_t T, int64_t D, int64_t R, int64_t W, int64_t G,
+                                              int dtype, int has_static) {
+  const int Rk = (int)R + (has_static ? 1 : 0);
+  if (B * T == 0 || G < 1 || G > kMaxGroups) return 0;
+  size_t tc = 0;
+  if (lr_tc_bwd_supported(D, Rk, (int)W, dtype, nullptr, 0, (int)G)) tc = lr_tc_bwd_workspace(B, T, D, Rk, (int)W, (int)G);
+  if (G > 1) return tc;
+  // Sized for whichever path dynconv_lr_bwd will take (pointer alignment aside,
+  // which only ever moves a call onto the simple path; both fit the max).
+  const size_t simple = align_up((size_t)lr_simple_partial_rows(B, T) * (size_t)Rk * (size_t)W * (size_t)D * sizeof(float));
+  return simple > tc ? simple : tc;
 }
 
 size_t dynconv_lr_bwd_workspace_bytes(int64_t B, int64_t T, int64_t D, int64_t R, int64_t W, int dtype,
                                       int has_static) {
-  const int Rk = (int)R + (has_static ? 1 : 0);
-  if (B * T == 0) return 0;
-  // Sized for whichever path dynconv_lr_bwd will take (pointer alignment aside,
-  // which only ever moves a call onto the simple path; both fit the max).
-  const size_t simple = align_up((size_t)lr_simple_partial_rows(B, T) * (size_t)Rk * (size_t)W * (size_t)D * sizeof(float));
-  size_t tc = 0;
-  if (lr_tc_bwd_supported(D, Rk, (int)W, dtype, nullptr, 0)) tc = lr_tc_bwd_workspace(B, T, D, Rk, (int)W);
-  return simple > tc ? simple : tc;
+  return dynconv_lr_bwd_grouped_workspace_bytes(B, T, D, R, W, 1, dtype, has_static);
 }
 
-int dynconv_lr_bwd(const void* x, const void* z, const void* U, const void* static_w, const void* dy, void* dx,
-                   void* dz, void* dU, void* dstatic_w, float* dU_f32, void* workspace, size_t workspace_bytes,
-                   int64_t B, int64_t T, int64_t D, int64_t R, int64_t W, int dtype, int residual, void* stream) {
+// dU_f32 [G][Rk][W*D] -> dU [G][R][W*D] and dstatic_w [G][W][D] (either may be null).
+static int cast_grouped(const float* dU_f32, void* dU, void* dsw, int64_t G, int64_t R, int Rk, int64_t W, int64_t D,
+                        int dtype, cudaStream_t st) {
+  int s;
+  const int64_t wd = W * D;
+  const size_t esz = dtype == DYNCONV_DTYPE_BF16 ? 2 : 4;
+  for (int64_t g = 0; g < G; ++g) {
+    const float* src = dU_f32 + g * Rk * wd;
+    if (dU && (s = cast_f32_launch(src, (char*)dU + (size_t)(g * R * wd) * esz, R * wd, dtype, st))) return s;
+    if (Rk > R && dsw && (s = cast_f32_launch(src + R * wd, (char*)dsw + (size_t)(g * wd) * esz, wd, dtype, st)))
+      return s;
+  }
+  return DYNCONV_OK;
+}
+
+int dynconv_lr_bwd_grouped(const void* x, const void* z, const void* U, const void* static_w, const void* dy,
+                           void* dx, void* dz, void* dU, void* dstatic_w, float* dU_f32, void* workspace,
+                           size_t workspace_bytes, int64_t B, int64_t T, int64_t D, int64_t R, int64_t W, int64_t G,
+                           int dtype, int residual, void* stream) {
   int s;
   if ((s = lr_checks(B, T, D, R, W, dtype))) return s;
+  if ((s = check_groups(G))) return s;
   const bool has_static = static_w != nullptr;
   const int Rk = (int)R + (has_static ? 1 : 0);
   if (Rk > 64) return set_error(DYNCONV_ERR_UNSUPPORTED, "R_kernel=%d > 64", Rk);
   if (!dU_f32) return set_error(DYNCONV_ERR_ARGUMENT, "lr_bwd: dU_f32 required");
   cudaStream_t st = (cudaStream_t)stream;
-  const int64_t nacc = (int64_t)Rk * W * D;
+  const int64_t nacc = G * Rk * W * D;
   if (B * T == 0) {
     if (cudaMemsetAsync(dU_f32, 0, (size_t)nacc * sizeof(float), st) != cudaSuccess)
       return set_error(DYNCONV_ERR_CUDA, "memset");
-    if (dU && (s = cast_f32_launch(dU_f32, dU, R * W * D, dtype, st))) return s;
-    if (has_static && dstatic_w && (s = cast_f32_launch(dU_f32 + R * W * D, dstatic_w, W * D, dtype, st))) return s;
-    return DYNCONV_OK;
+    return cast_grouped(dU_f32, dU, has_static ? dstatic_w : nullptr, G, R, Rk, W, D, dtype, st);
   }
   if (!x || !z || !U || !dy || !dx || !dz) return set_error(DYNCONV_ERR_ARGUMENT, "lr_bwd: null tensor");
-  const size_t need = dynconv_lr_bwd_workspace_bytes(B, T, D, R, W, dtype, has_static);
+  const void* ptrs[] = {x, z, U, static_w, dy, dx, dz};
+  const bool tc = lr_tc_bwd_supported(D, Rk, (int)W, dtype, ptrs, 7, (int)G);
+  if (!tc && G > 1)
+    return set_error(DYNCONV_ERR_UNSUPPORTED,
+                     "lr_bwd_grouped: G=%lld groups need the tensor-core path (bf16, W <= 4, R_kernel <= 32, "
+                     "D %% 128 == 0, G*D/128 <= SM count, 16-byte aligned tensors); call dynconv_lr_bwd per group",
+                     (long long)G);
+  const size_t need = dynconv_lr_bwd_grouped_workspace_bytes(B, T, D, R, W, G, dtype, has_static);
   if (!workspace || workspace_bytes < need)
     return set_error(DYNCONV_ERR_WORKSPACE, "lr_bwd: workspace %zu < %zu bytes", workspace_bytes, need);
-  const void* ptrs[] = {x, z, U, static_w, dy, dx, dz};
-  if (lr_tc_bwd_supported(D, Rk, (int)W, dtype, ptrs, 7))
+  if (tc)
     return lr_tc_bwd_launch(x, z, U, static_w, dy, dx, dz, dU_f32, dU, dstatic_w, workspace, workspace_bytes, B, T, D,
-                            (int)R, Rk, (int)W, residual, st);
+                            (int)G, (int)R, Rk, (int)W, residual, st);
   float* part = (float*)workspace;
   if ((s = lr_bwd_simple_launch(x, z, U, static_w, dy, dx, dz, part, B, T, D, (int)R, Rk, (int)W, dtype, residual, st)))
     return s;
   const int P = (int)lr_simple_partial_rows(B, T);
   if ((s = reduce_partials_launch(part, P, nacc, dU_f32, nullptr, dtype, st))) return s;
-  if (dU && (s = cast_f32_launch(dU_f32, dU, R * W * D, dtype, st))) return s;
-  if (has_static && dstatic_w && (s = cast_f32_launch(dU_f32 + R * W * D, dstatic_w, W * D, dtype, st))) return s;
-  return DYNCONV_OK;
+  return cast_grouped(dU_f32, dU, has_static ? dstatic_w : nullptr, 1, R, Rk, W, D, dtype, st);
+}
+
+int dynconv_lr_bwd(const void* x, const void* z, const void* U, const void* static_w, const void* dy, void* dx,
+                   void* dz, void* dU, void* dstatic_w, float* dU_f32, void* workspace, size_t workspace_bytes,
+                   int64_t B, int64_t T, int64_t D, int64_t R, int64_t W, int dtype, int residual, void* stream) {
+  return dynconv_lr_bwd_grouped(x, z, U, static_w, dy, dx, dz, dU, dstatic_w, dU_f32, workspace, workspace_bytes, B,
+                                T, D, R, W, 1, dtype, residual, stream);
 }
 
 int dynconv_cast_f32(const float* src, void* dst, int64_t n, int dtype, void* stream) {
@@ -356,10 +413,11 @@ int dynconv_cast_f32(const float* src, void* dst, int64_t n, int dtype, void* st
 }
 
 int dynconv_umma_selftest(const void* A, const void* B, float* D, int M, int N, int K, int Nb, int a_major, int a_sbo,
-                          int a_lbo, int b_major, int b_sbo, int b_lbo, int b_row_offset, void* stream) {
+                          int a_lbo, int b_major, int b_sbo, int b_lbo, int b_row_offset, int a_row_offset,
+                          void* stream) {
   if (!A || !B || !D) return set_error(DYNCONV_ERR_ARGUMENT, "selftest: null pointer");
   return umma_selftest_launch(A, B, D, M, N, K, Nb, a_major, a_sbo, a_lbo, b_major, b_sbo, b_lbo, b_row_offset,
-                              (cudaStream_t)stream);
+                              a_row_offset, (cudaStream_t)stream);
 }
 
 int dynconv_wait_selftest(uint64_t limit_ns, int* out, void* stream) {

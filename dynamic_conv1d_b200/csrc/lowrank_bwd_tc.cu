@@ -153,7 +153,9 @@ __global__ void __launch_bounds__(kThreads, 1)
                      const __grid_constant__ CUtensorMap zmap, const __nv_bfloat16* __restrict__ U,
                      const __nv_bfloat16* __restrict__ sw, __nv_bfloat16* __restrict__ dx, __nv_bfloat16* __restrict__ dz, float* __restrict__ dzp, int* __restrict__ grp_done,
                      float* __restrict__ dUp, float* __restrict__ dU_f32, __nv_bfloat16* __restrict__ dU,
-                     __nv_bfloat16* __restrict__ dsw, TileSplit sp, int T, int D, int R, int Rk, int residual, int tma4) {
+                     __nv_bfloat16* __restrict__ dsw, TileSplit sp, ChanGroups cg, int T, int D, int R, int Rk,
+                     int residual, int tma4) {
+  // D: channels of an activation row (G * Dg); cg.Dg: channels of one group's U
   using L = BwdCfg<W, RKP>;
   constexpr int S = L::S, NP = L::NP, kTRing = L::kTRing;
   constexpr int kW0 = (W + 1) / 2;  // taps [0, kW0) go to the first issuer of a split stream
@@ -172,7 +174,9 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int j1 = (int)((int64_t)sp.n_tiles * (g + 1) / sp.n_groups);
   const int n = j1 - j0;
   const int nq = n * kQPT;
-  const int d0 = dblk * kBD;
+  const int d0 = dblk * kBD;           // first channel in the activation row
+  const int grp = dblk / cg.nd;        // channel group of this CTA's block
+  const int dl0 = d0 - grp * cg.Dg;    // first channel within the group
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < S; ++s) {
@@ -214,7 +218,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     // the 16x16 identity (transpose B operand), TMEM allocation, U^T in TMEM.
     constexpr int kNonProducer = kThreads - 32;
     const int tid = threadIdx.x - 32;
-    load_u_block<W, RKP, kNonProducer>(smem + L::kOffU, U, sw, dblk, D, R, tid);
+    load_u_block<W, RKP, kNonProducer>(smem + L::kOffU, U + (size_t)grp * R * W * cg.Dg,
+                                       sw ? sw + (size_t)grp * W * cg.Dg : nullptr, dblk - grp * cg.nd, cg.Dg, R, tid);
     if (tid < kQ * kQ) {
       const int nn = tid >> 4, kk = tid & 15;
       *reinterpret_cast<__nv_bfloat16*>(smem + L::kOffI + kmajor_off(nn, kk, 128, 256)) =
@@ -244,7 +249,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int tile = j0 + k, b = tile / sp.tiles_row, t0 = (tile % sp.tiles_row) * kBT;
         if (!mbar_wait(&zempty[k & 1], ((k >> 1) & 1) ^ 1, kErrWaitProducer, &abort_flag)) break;
         mbar_arrive_expect_tx(&zfull[k & 1], L::kZBytes);
-        tma_load_4d(smem + L::kOffZ + (k & 1) * L::kZStride, &zmap, &zfull[k & 1], 0, t0, b, 0, pol);
+        tma_load_4d(smem + L::kOffZ + (k & 1) * L::kZStride, &zmap, &zfull[k & 1], 0, t0, b, grp * (RKP / 8), pol);
         bool ok = true;
         for (int bb = 0; bb < kBlkPT; ++bb) {
           const int nb = kBlkPT * k + bb, m = nb % S;
@@ -525,7 +530,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
     }
     if (n >= 1) dz_readout(n - 1);
-    // dU partial of this CTA: TMEM (lane = channel) -> dUp[g][r][w*D + d0 + ch]
+    // dU partial of this CTA: TMEM (lane = channel) -> dUp[g][grp][r][w*Dg + dl0 + ch]
     if (!dead) dead = !mbar_wait(&du_bar, 0, kErrWaitTail, &abort_flag);
     tc_fence_after();
     if (!dead) {
@@ -537,7 +542,8 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
         for (int c = 0; c < 16; ++c) {
           const int r = rc * 16 + c;
-          if (r < Rk && dok) dUp[((size_t)g * Rk + r) * W * D + (size_t)w * D + d0 + ch] = v[c];
+          if (r < Rk && dok)
+            dUp[(((size_t)g * cg.G + grp) * Rk + r) * W * cg.Dg + (size_t)w * cg.Dg + dl0 + ch] = v[c];
         }
       }
     }
@@ -571,17 +577,23 @@ __global__ void __launch_bounds__(kThreads, 1)
   }
   __syncthreads();
   if (grp_ok) {
-    const int64_t nsteps = (int64_t)n * kBT;
-    const int64_t lo = nsteps * dblk / sp.n_dblk, hi = nsteps * (dblk + 1) / sp.n_dblk;
+    // (step, channel group) pairs of the token group, split evenly over its CTAs;
+    // group go's dz sums the partials of its own channel blocks
+    const int64_t npairs = (int64_t)n * kBT * cg.G;
+    const int64_t lo = npairs * dblk / sp.n_dblk, hi = npairs * (dblk + 1) / sp.n_dblk;
     constexpr int RQ = RKP / 4;  // float4 groups per step
+    const int RG = cg.G * R;     // dz row width
     for (int64_t e2 = lo * RQ + threadIdx.x; e2 < hi * RQ; e2 += blockDim.x) {
-      const int64_t st = e2 / RQ;
+      const int64_t sg = e2 / RQ;
       const int rq = (int)(e2 % RQ);
+      const int64_t st = sg / cg.G;
+      const int go = (int)(sg - st * cg.G);
       const int tile = j0 + (int)(st / kBT), tok = (int)(st % kBT);
       const int b = tile / sp.tiles_row, t = (tile % sp.tiles_row) * kBT + tok;
       float4 a4 = make_float4(0.f, 0.f, 0.f, 0.f);
+      const int kb = go * cg.nd;
 #pragma unroll 4
-      for (int k2 = 0; k2 < sp.n_dblk; ++k2) {  // partial loads in flight, summed in order
+      for (int k2 = kb; k2 < kb + cg.nd; ++k2) {  // partial loads in flight, summed in order
         const float4 f =
             __ldcg(reinterpret_cast<const float4*>(dzp + (((size_t)k2 * sp.n_tiles + tile) * kBT + tok) * RKP) + rq);
         a4.x += f.x;
@@ -590,7 +602,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         a4.w += f.w;
       }
       if (t < T) {
-        __nv_bfloat16* dst = dz + ((size_t)b * T + t) * R;
+        __nv_bfloat16* dst = dz + ((size_t)b * T + t) * RG + go * R;
         const float av[4] = {a4.x, a4.y, a4.z, a4.w};
 #pragma unroll
         for (int c = 0; c < 4; ++c)
@@ -623,8 +635,9 @@ __global__ void __launch_bounds__(kThreads, 1)
   }
   __syncthreads();
   if (grp_ok) {
-    const int64_t wd = (int64_t)W * D;
-    const int64_t n4 = (int64_t)Rk * wd / 4;  // W*D % 4 == 0 (D % 8 == 0)
+    const int64_t wd = (int64_t)W * cg.Dg;
+    const int64_t per_g = (int64_t)Rk * wd;  // one group's [Rk][W*Dg] block
+    const int64_t n4 = cg.G * per_g / 4;     // W*Dg % 4 == 0 (Dg % 8 == 0)
     const int64_t lo = n4 * blockIdx.x / gridDim.x, hi = n4 * (blockIdx.x + 1) / gridDim.x;
     for (int64_t i = lo + threadIdx.x; i < hi; i += blockDim.x) {
       float4 a4 = make_float4(0.f, 0.f, 0.f, 0.f);
@@ -638,8 +651,12 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       reinterpret_cast<float4*>(dU_f32)[i] = a4;
       const int64_t e0 = 4 * i;
-      const int r = (int)(e0 / wd);
-      __nv_bfloat16* dst = r < R ? (dU ? dU + e0 : nullptr) : (dsw ? dsw + (e0 - (int64_t)R * wd) : nullptr);
+      const int go = (int)(e0 / per_g);
+      const int64_t rem = e0 - go * per_g;
+      const int r = (int)(rem / wd);
+      const int64_t col = rem - (int64_t)r * wd;
+      __nv_bfloat16* dst = r < R ? (dU ? dU + ((int64_t)go * R + r) * wd + col : nullptr)
+                                 : (dsw ? dsw + (int64_t)go * wd + col : nullptr);
       if (dst) {
         dst[0] = __float2bfloat16_rn(a4.x);
         dst[1] = __float2bfloat16_rn(a4.y);
@@ -665,14 +682,15 @@ size_t al256(size_t v) { return (v + 255) / 256 * 256; }
 
 int rkp_of(int Rk) { return Rk <= 16 ? 16 : 32; }
 
-BwdWorkspace bwd_workspace(void* base, int64_t B, int64_t T, int64_t D, int Rk, int W) {
-  const TileSplit sp = tile_split(B, T, D);
+// D: channels per group; the activation rows hold G * D.
+BwdWorkspace bwd_workspace(void* base, int64_t B, int64_t T, int64_t D, int Rk, int W, int G) {
+  const TileSplit sp = tile_split(B, T, (int64_t)G * D);
   const int rkp = rkp_of(Rk);
   BwdWorkspace w;
   const size_t dzp = al256((size_t)sp.n_dblk * sp.n_tiles * kBT * rkp * sizeof(float));
   const size_t cnt = al256((size_t)(sp.n_groups + 1) * sizeof(int));  // group counts + grid count
-  const size_t dUp = al256((size_t)sp.n_groups * Rk * W * D * sizeof(float));
-  const size_t zp = zpack_bytes(B, T, rkp);
+  const size_t dUp = al256((size_t)sp.n_groups * G * Rk * W * D * sizeof(float));
+  const size_t zp = zpack_bytes(B, T, rkp, G);
   uint8_t* p = (uint8_t*)base;
   w.dzp = (float*)p;
   w.cnt = (int*)(p ? p + dzp : nullptr);
@@ -682,25 +700,29 @@ BwdWorkspace bwd_workspace(void* base, int64_t B, int64_t T, int64_t D, int Rk, 
   return w;
 }
 
+// x, dy, dx: [B][T][G*D]; z, dz: [B][T][G*R]; U, dU: [G][R][W*D]; sw, dsw: [G][W][D];
+// dU_f32: [G][Rk][W*D].
 template <int W, int RKP>
 int launch_bwd(const void* x, const void* z, const void* U, const void* sw, const void* dy, void* dx, void* dz,
-               float* dU_f32, void* dU, void* dsw, void* wsp, int64_t B, int64_t T, int64_t D, int R, int Rk,
+               float* dU_f32, void* dU, void* dsw, void* wsp, int64_t B, int64_t T, int64_t D, int G, int R, int Rk,
                int residual, cudaStream_t st) {
   using L = BwdCfg<W, RKP>;
   CUtensorMap dymap, xmap, zmap;
   int s;
-  const TileSplit sp = tile_split(B, T, D);
-  BwdWorkspace ws = bwd_workspace(wsp, B, T, D, Rk, W);
-  const int tma4 = D % 64 == 0 ? 1 : 0;
+  const int64_t Dt = (int64_t)G * D;
+  const TileSplit sp = tile_split(B, T, Dt);
+  const ChanGroups cg = chan_groups(D, G);
+  BwdWorkspace ws = bwd_workspace(wsp, B, T, D, Rk, W, G);
+  const int tma4 = Dt % 64 == 0 ? 1 : 0;
   if (tma4) {
-    if ((s = make_btd4_map(&dymap, dy, B, T, D, kQ))) return s;
-    if ((s = make_btd4_map(&xmap, x, B, T, D, kQ))) return s;
+    if ((s = make_btd4_map(&dymap, dy, B, T, Dt, kQ))) return s;
+    if ((s = make_btd4_map(&xmap, x, B, T, Dt, kQ))) return s;
   } else {
-    if ((s = make_btd_map(&dymap, dy, B, T, D, 64, kQ, true))) return s;
-    if ((s = make_btd_map(&xmap, x, B, T, D, 64, kQ, true))) return s;
+    if ((s = make_btd_map(&dymap, dy, B, T, Dt, 64, kQ, true))) return s;
+    if ((s = make_btd_map(&xmap, x, B, T, Dt, 64, kQ, true))) return s;
   }
-  if ((s = make_zpack_map(&zmap, ws.zp, B, T, RKP, kZRows))) return s;
-  if ((s = z_pack_launch(z, ws.zp, B, T, R, RKP, sw != nullptr, st))) return s;
+  if ((s = make_zpack_map(&zmap, ws.zp, B, T, RKP, kZRows, G))) return s;
+  if ((s = z_pack_launch(z, ws.zp, B, T, R, RKP, sw != nullptr, st, G))) return s;
   cudaError_t e = cudaMemsetAsync(ws.cnt, 0, (size_t)(sp.n_groups + 1) * sizeof(int), st);
   if (e != cudaSuccess) return cuda_status(e, "cudaMemsetAsync(group counters)");
   const int smem = (int)L::kTotal;
@@ -724,7 +746,8 @@ int launch_bwd(const void* x, const void* z, const void* U, const void* sw, cons
   cfg.numAttrs = 1;
   e = cudaLaunchKernelEx(&cfg, lr_bwd_tc_kernel<W, RKP>, dymap, xmap, zmap, (const __nv_bfloat16*)U,
                          (const __nv_bfloat16*)sw, (__nv_bfloat16*)dx, (__nv_bfloat16*)dz, ws.dzp, ws.cnt, ws.dUp, dU_f32,
-                         (__nv_bfloat16*)dU, (__nv_bfloat16*)(sw ? dsw : nullptr), sp, (int)T, (int)D, R, Rk, residual, tma4);
+                         (__nv_bfloat16*)dU, (__nv_bfloat16*)(sw ? dsw : nullptr), sp, cg, (int)T, (int)Dt, R, Rk,
+                         residual, tma4);
   if (e != cudaSuccess) {
     cudaGetLastError();
     return cuda_status(e, "cudaLaunchKernelEx(lr_bwd_tc_kernel)");
@@ -735,13 +758,13 @@ int launch_bwd(const void* x, const void* z, const void* U, const void* sw, cons
 
 template <int RKP>
 int launch_bwd_w(int W, const void* x, const void* z, const void* U, const void* sw, const void* dy, void* dx,
-                 void* dz, float* dU_f32, void* dU, void* dsw, void* ws, int64_t B, int64_t T, int64_t D, int R,
+                 void* dz, float* dU_f32, void* dU, void* dsw, void* ws, int64_t B, int64_t T, int64_t D, int G, int R,
                  int Rk, int residual, cudaStream_t st) {
   switch (W) {
-    case 1: return launch_bwd<1, RKP>(x, z, U, sw, dy, dx, dz, dU_f32, dU, dsw, ws, B, T, D, R, Rk, residual, st);
-    case 2: return launch_bwd<2, RKP>(x, z, U, sw, dy, dx, dz, dU_f32, dU, dsw, ws, B, T, D, R, Rk, residual, st);
-    case 3: return launch_bwd<3, RKP>(x, z, U, sw, dy, dx, dz, dU_f32, dU, dsw, ws, B, T, D, R, Rk, residual, st);
-    case 4: return launch_bwd<4, RKP>(x, z, U, sw, dy, dx, dz, dU_f32, dU, dsw, ws, B, T, D, R, Rk, residual, st);
+    case 1: return launch_bwd<1, RKP>(x, z, U, sw, dy, dx, dz, dU_f32, dU, dsw, ws, B, T, D, G, R, Rk, residual, st);
+    case 2: return launch_bwd<2, RKP>(x, z, U, sw, dy, dx, dz, dU_f32, dU, dsw, ws, B, T, D, G, R, Rk, residual, st);
+    case 3: return launch_bwd<3, RKP>(x, z, U, sw, dy, dx, dz, dU_f32, dU, dsw, ws, B, T, D, G, R, Rk, residual, st);
+    case 4: return launch_bwd<4, RKP>(x, z, U, sw, dy, dx, dz, dU_f32, dU, dsw, ws, B, T, D, G, R, Rk, residual, st);
     default: return set_error(DYNCONV_ERR_UNSUPPORTED, "tensor-core backward: W=%d", W);
   }
 }
@@ -749,27 +772,30 @@ int launch_bwd_w(int W, const void* x, const void* z, const void* U, const void*
 }  // namespace
 
 // Tensor-core backward envelope: bf16, W <= 4, R_kernel <= 32, D % 8 == 0 (TMA row
-// pitch), 16-byte aligned activations (TMA base), grid co-resident.  Everything
-// else runs the CUDA-core kernels of lowrank_simple.cu.
-bool lr_tc_bwd_supported(int64_t D, int Rk, int W, int dtype, const void* const* ptrs, int nptrs) {
+// pitch; D % 128 == 0 with G > 1 channel groups), 16-byte aligned activations (TMA
+// base), grid co-resident.  Everything else runs the CUDA-core kernels of
+// lowrank_simple.cu (G = 1 only).
+bool lr_tc_bwd_supported(int64_t D, int Rk, int W, int dtype, const void* const* ptrs, int nptrs, int G) {
   if (dtype != DYNCONV_DTYPE_BF16 || W < 1 || W > 4 || Rk < 1 || Rk > 32 || D % 8 != 0) return false;
-  if ((D + kBD - 1) / kBD > sm_count()) return false;  // the cooperative grid must fit on the GPU
+  if (G < 1 || (G > 1 && D % kBD != 0)) return false;
+  if (((int64_t)G * D + kBD - 1) / kBD > sm_count()) return false;  // the cooperative grid must fit on the GPU
   for (int i = 0; i < nptrs; ++i)
     if (ptrs[i] && !aligned16(ptrs[i])) return false;
   return encode_fn() != nullptr || nptrs == 0;
 }
 
-size_t lr_tc_bwd_workspace(int64_t B, int64_t T, int64_t D, int Rk, int W) {
-  return bwd_workspace(nullptr, B, T, D, Rk, W).bytes;
+size_t lr_tc_bwd_workspace(int64_t B, int64_t T, int64_t D, int Rk, int W, int G) {
+  return bwd_workspace(nullptr, B, T, D, Rk, W, G).bytes;
 }
 
 int lr_tc_bwd_launch(const void* x, const void* z, const void* U, const void* sw, const void* dy, void* dx, void* dz,
                      float* dU_f32, void* dU, void* dsw, void* ws, size_t ws_bytes, int64_t B, int64_t T, int64_t D,
-                     int R, int Rk, int W, int residual, cudaStream_t st) {
-  if (ws_bytes < lr_tc_bwd_workspace(B, T, D, Rk, W))
+                     int G, int R, int Rk, int W, int residual, cudaStream_t st) {
+  if (ws_bytes < lr_tc_bwd_workspace(B, T, D, Rk, W, G))
     return set_error(DYNCONV_ERR_WORKSPACE, "lr_bwd (tensor core): workspace too small");
-  if (Rk <= 16) return launch_bwd_w<16>(W, x, z, U, sw, dy, dx, dz, dU_f32, dU, dsw, ws, B, T, D, R, Rk, residual, st);
-  return launch_bwd_w<32>(W, x, z, U, sw, dy, dx, dz, dU_f32, dU, dsw, ws, B, T, D, R, Rk, residual, st);
+  if (Rk <= 16)
+    return launch_bwd_w<16>(W, x, z, U, sw, dy, dx, dz, dU_f32, dU, dsw, ws, B, T, D, G, R, Rk, residual, st);
+  return launch_bwd_w<32>(W, x, z, U, sw, dy, dx, dz, dU_f32, dU, dsw, ws, B, T, D, G, R, Rk, residual, st);
 }
 
 }  // namespace dynconv

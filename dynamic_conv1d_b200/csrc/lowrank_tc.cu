@@ -82,11 +82,11 @@ int make_btd4_map(CUtensorMap* map, const void* base, int64_t B, int64_t T, int6
   return DYNCONV_OK;
 }
 
-int make_zpack_map(CUtensorMap* map, const void* base, int64_t B, int64_t T, int rkp, int rows) {
+int make_zpack_map(CUtensorMap* map, const void* base, int64_t B, int64_t T, int rkp, int rows, int G) {
   EncodeTiledFn fn = encode_fn();
   if (!fn) return set_error(DYNCONV_ERR_CUDA, "cuTensorMapEncodeTiled unavailable");
   if (int s = ensure_context()) return s;
-  cuuint64_t dims[4] = {8, (cuuint64_t)T, (cuuint64_t)B, (cuuint64_t)(rkp / 8)};
+  cuuint64_t dims[4] = {8, (cuuint64_t)T, (cuuint64_t)B, (cuuint64_t)(G * rkp / 8)};
   cuuint64_t strides[3] = {16, (cuuint64_t)T * 16, (cuuint64_t)B * T * 16};
   cuuint32_t box[4] = {8, (cuuint32_t)rows, 1, (cuuint32_t)(rkp / 8)};
   cuuint32_t estr[4] = {1, 1, 1, 1};
@@ -97,18 +97,20 @@ int make_zpack_map(CUtensorMap* map, const void* base, int64_t B, int64_t T, int
   return DYNCONV_OK;
 }
 
-// z_pack[c][b][t][e] = z_ext[b, t, 8c + e]: z for ranks < R, 1.0 at rank R when the
-// static filter is fused (the reference's F.pad(z, (0, 1), value=1.0),
-// lowrank.py:224), 0 up to RKP.  One thread per (8-rank chunk, token): consecutive
-// threads write consecutive 16-byte chunks.
+// z_pack[g*RKP/8 + c][b][t][e] = z_ext_g[b, t, 8c + e]: group g's z (columns
+// g*R .. g*R+R-1 of a [B][T][G*R] row) for ranks < R, 1.0 at rank R when the static
+// filter is fused (the reference's F.pad(z, (0, 1), value=1.0), lowrank.py:224), 0 up
+// to RKP.  One thread per (8-rank chunk, token): consecutive threads write
+// consecutive 16-byte chunks.
 __global__ void __launch_bounds__(256) z_pack_kernel(const __nv_bfloat16* __restrict__ z,
                                                      __nv_bfloat16* __restrict__ zp, int64_t ntok, int R, int rkp,
-                                                     int has_static) {
+                                                     int has_static, int G) {
   const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
-  if (i >= ntok * (rkp / 8)) return;
-  const int c = (int)(i / ntok);
-  const int64_t tok = i - (int64_t)c * ntok;
-  const __nv_bfloat16* zr = z + tok * R;
+  if (i >= ntok * (G * rkp / 8)) return;
+  const int cc = (int)(i / ntok);
+  const int64_t tok = i - (int64_t)cc * ntok;
+  const int g = cc / (rkp / 8), c = cc - g * (rkp / 8);
+  const __nv_bfloat16* zr = z + tok * (int64_t)(G * R) + g * R;
   __align__(16) __nv_bfloat16 v[8];
 #pragma unroll
   for (int e = 0; e < 8; ++e) {
@@ -118,13 +120,16 @@ __global__ void __launch_bounds__(256) z_pack_kernel(const __nv_bfloat16* __rest
   *reinterpret_cast<uint4*>(zp + i * 8) = *reinterpret_cast<const uint4*>(v);
 }
 
-size_t zpack_bytes(int64_t B, int64_t T, int rkp) { return ((size_t)B * T * rkp * 2 + 255) / 256 * 256; }
+size_t zpack_bytes(int64_t B, int64_t T, int rkp, int G) {
+  return ((size_t)B * T * rkp * G * 2 + 255) / 256 * 256;
+}
 
-int z_pack_launch(const void* z, void* zp, int64_t B, int64_t T, int R, int rkp, bool has_static, cudaStream_t st) {
+int z_pack_launch(const void* z, void* zp, int64_t B, int64_t T, int R, int rkp, bool has_static, cudaStream_t st,
+                  int G) {
   const int64_t ntok = B * T;
-  const int64_t nthreads = ntok * (rkp / 8);
+  const int64_t nthreads = ntok * (G * rkp / 8);
   z_pack_kernel<<<(unsigned)((nthreads + 255) / 256), 256, 0, st>>>((const __nv_bfloat16*)z, (__nv_bfloat16*)zp,
-                                                                   ntok, R, rkp, has_static ? 1 : 0);
+                                                                   ntok, R, rkp, has_static ? 1 : 0, G);
   DYNCONV_CHECK_LAUNCH("z_pack_kernel");
   return DYNCONV_OK;
 }
@@ -169,7 +174,7 @@ template <int W, int RKP>
 __global__ void __launch_bounds__(kFwdThreads, 1)
     lr_fwd_tc_kernel(const __grid_constant__ CUtensorMap xmap, const __grid_constant__ CUtensorMap ymap,
                      const __grid_constant__ CUtensorMap zmap, const __nv_bfloat16* __restrict__ U,
-                     const __nv_bfloat16* __restrict__ sw, TileSplit sp, int T, int D, int R, int residual) {
+                     const __nv_bfloat16* __restrict__ sw, TileSplit sp, ChanGroups cg, int T, int R, int residual) {
   using L = FwdSmem<W, RKP>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = align_smem_1024(smem_raw);
@@ -184,6 +189,7 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
   const int j0 = (int)((int64_t)sp.n_tiles * g / sp.n_groups);
   const int n = (int)((int64_t)sp.n_tiles * (g + 1) / sp.n_groups) - j0;
   const int d0 = dblk * kBD;
+  const int grp = dblk / cg.nd;  // channel group of this CTA's block
   constexpr uint32_t kAccCols = W * kBT;
   constexpr uint32_t kTmemCols = (2 * kAccCols <= 256) ? 256 : 512;
 
@@ -210,7 +216,9 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
     // U block of this CTA's channels (MMA A operand), loaded once by all but the
     // producer, then the TMEM allocation.
     constexpr int kNonProducer = kFwdThreads - 32;
-    load_u_block<W, RKP, kNonProducer>(smem + L::kOffU, U, sw, dblk, D, R, threadIdx.x - 32);
+    load_u_block<W, RKP, kNonProducer>(smem + L::kOffU, U + (size_t)grp * R * W * cg.Dg,
+                                       sw ? sw + (size_t)grp * W * cg.Dg : nullptr, dblk - grp * cg.nd, cg.Dg, R,
+                                       threadIdx.x - 32);
     fence_proxy_async_smem();
     if (warp == 1) {
       tmem_alloc(&tmem_slot, kTmemCols);
@@ -232,7 +240,7 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
         const int tile = j0 + k, b = tile / sp.tiles_row, t0 = (tile % sp.tiles_row) * kBT;
         mbar_arrive_expect_tx(&full_bar[s], L::kXBytes + L::kZBytes);
         tma_load_3d(smem + L::kOffX + s * L::kXStride, &xmap, &full_bar[s], d0, t0 - (W - 1), b, pol);
-        tma_load_4d(smem + L::kOffZ + s * L::kZBytes, &zmap, &full_bar[s], 0, t0, b, 0, pol);
+        tma_load_4d(smem + L::kOffZ + s * L::kZBytes, &zmap, &full_bar[s], 0, t0, b, grp * (RKP / 8), pol);
       }
     }
     __syncwarp();
@@ -328,18 +336,21 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
   if (warp == 1) tmem_dealloc(tmem, kTmemCols);
 }
 
+// x, y: [B][T][G*D]; z: [B][T][G*R]; U: [G][R][W*D]; sw: [G][W][D] or null.
 template <int W, int RKP>
 int launch_fwd(const void* x, const void* z, const void* U, const void* sw, void* y, void* ws, int64_t B, int64_t T,
-               int64_t D, int R, int residual, cudaStream_t st) {
+               int64_t D, int G, int R, int residual, cudaStream_t st) {
   using L = FwdSmem<W, RKP>;
   static_assert(L::kTotal <= 232448 - 512, "forward shared memory budget (227 KB per CTA)");
+  const int64_t Dt = (int64_t)G * D;
   CUtensorMap xmap, ymap, zmap;
   int s;
-  if ((s = make_btd_map(&xmap, x, B, T, D, kBD, kBT + W - 1))) return s;
-  if ((s = make_btd_map(&ymap, y, B, T, D, 32, kEpiSteps))) return s;  // per-warp [steps][32 ch] stores
-  if ((s = make_zpack_map(&zmap, ws, B, T, RKP, kBT))) return s;
-  if ((s = z_pack_launch(z, ws, B, T, R, RKP, sw != nullptr, st))) return s;
-  const TileSplit sp = tile_split(B, T, D);
+  if ((s = make_btd_map(&xmap, x, B, T, Dt, kBD, kBT + W - 1))) return s;
+  if ((s = make_btd_map(&ymap, y, B, T, Dt, 32, kEpiSteps))) return s;  // per-warp [steps][32 ch] stores
+  if ((s = make_zpack_map(&zmap, ws, B, T, RKP, kBT, G))) return s;
+  if ((s = z_pack_launch(z, ws, B, T, R, RKP, sw != nullptr, st, G))) return s;
+  const TileSplit sp = tile_split(B, T, Dt);
+  const ChanGroups cg = chan_groups(D, G);
   const int grid = sp.n_dblk * sp.n_groups;
   const int smem = (int)L::kTotal;
   cudaError_t e = cudaFuncSetAttribute(lr_fwd_tc_kernel<W, RKP>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
@@ -348,48 +359,50 @@ int launch_fwd(const void* x, const void* z, const void* U, const void* sw, void
     return cuda_status(e, "cudaFuncSetAttribute(lr_fwd_tc)");
   }
   lr_fwd_tc_kernel<W, RKP><<<grid, kFwdThreads, smem, st>>>(xmap, ymap, zmap, (const __nv_bfloat16*)U,
-                                                            (const __nv_bfloat16*)sw, sp, (int)T, (int)D, R, residual);
+                                                            (const __nv_bfloat16*)sw, sp, cg, (int)T, R, residual);
   DYNCONV_CHECK_LAUNCH("lr_fwd_tc_kernel");
   return DYNCONV_OK;
 }
 
 template <int RKP>
 int launch_fwd_w(int W, const void* x, const void* z, const void* U, const void* sw, void* y, void* ws, int64_t B,
-                 int64_t T, int64_t D, int R, int residual, cudaStream_t st) {
+                 int64_t T, int64_t D, int G, int R, int residual, cudaStream_t st) {
   switch (W) {
-    case 1: return launch_fwd<1, RKP>(x, z, U, sw, y, ws, B, T, D, R, residual, st);
-    case 2: return launch_fwd<2, RKP>(x, z, U, sw, y, ws, B, T, D, R, residual, st);
-    case 3: return launch_fwd<3, RKP>(x, z, U, sw, y, ws, B, T, D, R, residual, st);
-    case 4: return launch_fwd<4, RKP>(x, z, U, sw, y, ws, B, T, D, R, residual, st);
+    case 1: return launch_fwd<1, RKP>(x, z, U, sw, y, ws, B, T, D, G, R, residual, st);
+    case 2: return launch_fwd<2, RKP>(x, z, U, sw, y, ws, B, T, D, G, R, residual, st);
+    case 3: return launch_fwd<3, RKP>(x, z, U, sw, y, ws, B, T, D, G, R, residual, st);
+    case 4: return launch_fwd<4, RKP>(x, z, U, sw, y, ws, B, T, D, G, R, residual, st);
     default: return set_error(DYNCONV_ERR_UNSUPPORTED, "tensor-core path: W=%d", W);
   }
 }
 
-
 }  // namespace
 
 // Tensor-core forward envelope: bf16, W <= 4, R_kernel <= 64, D % 8 == 0 (TMA row
-// pitch), 16-byte aligned activations (TMA base).  Everything else runs the
-// CUDA-core kernels of lowrank_simple.cu.
-bool lr_tc_supported(int64_t D, int Rk, int W, int dtype, const void* const* ptrs, int nptrs) {
+// pitch; D % 128 == 0 with G > 1 channel groups), 16-byte aligned activations (TMA
+// base).  Everything else runs the CUDA-core kernels of lowrank_simple.cu.
+bool lr_tc_supported(int64_t D, int Rk, int W, int dtype, const void* const* ptrs, int nptrs, int G) {
   if (dtype != DYNCONV_DTYPE_BF16 || W < 1 || W > 4 || Rk < 1 || Rk > 64 || D % 8 != 0) return false;
+  if (G < 1 || (G > 1 && D % kBD != 0)) return false;
   for (int i = 0; i < nptrs; ++i)
     if (ptrs[i] && !aligned16(ptrs[i])) return false;
   return encode_fn() != nullptr || nptrs == 0;
 }
 
-size_t lr_tc_fwd_workspace(int64_t B, int64_t T, int Rk) { return zpack_bytes(B, T, (Rk + 15) / 16 * 16); }
+size_t lr_tc_fwd_workspace(int64_t B, int64_t T, int Rk, int G) {
+  return zpack_bytes(B, T, (Rk + 15) / 16 * 16, G);
+}
 
 int lr_tc_fwd_launch(const void* x, const void* z, const void* U, const void* sw, void* y, void* ws, size_t ws_bytes,
-                     int64_t B, int64_t T, int64_t D, int R, int Rk, int W, int residual, cudaStream_t st) {
-  if (!ws || ws_bytes < lr_tc_fwd_workspace(B, T, Rk))
+                     int64_t B, int64_t T, int64_t D, int G, int R, int Rk, int W, int residual, cudaStream_t st) {
+  if (!ws || ws_bytes < lr_tc_fwd_workspace(B, T, Rk, G))
     return set_error(DYNCONV_ERR_WORKSPACE, "lr_fwd (tensor core): workspace too small");
   const int rkp = (Rk + 15) / 16 * 16;
   switch (rkp) {
-    case 16: return launch_fwd_w<16>(W, x, z, U, sw, y, ws, B, T, D, R, residual, st);
-    case 32: return launch_fwd_w<32>(W, x, z, U, sw, y, ws, B, T, D, R, residual, st);
-    case 48: return launch_fwd_w<48>(W, x, z, U, sw, y, ws, B, T, D, R, residual, st);
-    case 64: return launch_fwd_w<64>(W, x, z, U, sw, y, ws, B, T, D, R, residual, st);
+    case 16: return launch_fwd_w<16>(W, x, z, U, sw, y, ws, B, T, D, G, R, residual, st);
+    case 32: return launch_fwd_w<32>(W, x, z, U, sw, y, ws, B, T, D, G, R, residual, st);
+    case 48: return launch_fwd_w<48>(W, x, z, U, sw, y, ws, B, T, D, G, R, residual, st);
+    case 64: return launch_fwd_w<64>(W, x, z, U, sw, y, ws, B, T, D, G, R, residual, st);
     default: return set_error(DYNCONV_ERR_UNSUPPORTED, "R_kernel=%d", Rk);
   }
 }

@@ -38,6 +38,19 @@ inline TileSplit tile_split(int64_t B, int64_t T, int64_t D) {
   return sp;
 }
 
+// Channel groups: G independent convolutions side by side in one activation row
+// ([B][T][G*Dg] -- the query, key and value slices of a fused QKV projection),
+// each with its own z slice ([B][T][G*R]) and its own U / static_w.  Group g owns
+// channel blocks [g*nd, (g+1)*nd); with G > 1, Dg % 128 == 0, so no 128-channel
+// block straddles two groups and a block's global first channel is dblk * 128.
+struct ChanGroups {
+  int G;   // number of groups (1 = the plain op)
+  int nd;  // channel blocks per group, ceil(Dg / 128)
+  int Dg;  // channels per group
+};
+
+inline ChanGroups chan_groups(int64_t D, int G) { return ChanGroups{G, (int)((D + kBD - 1) / kBD), (int)D}; }
+
 __host__ __device__ constexpr uint32_t round1024(uint32_t v) { return (v + 1023u) / 1024u * 1024u; }
 
 inline bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; }
@@ -60,13 +73,16 @@ int make_btd_map(CUtensorMap* map, const void* base, int64_t B, int64_t T, int64
 // bytes apart -- the layout two 3-D loads of 64 channels would produce.
 int make_btd4_map(CUtensorMap* map, const void* base, int64_t B, int64_t T, int64_t D, int box_t);
 
-// 4-D bf16 map over z_pack [RKP/8][B][T][8]: dims (8, T, B, RKP/8), box (8, rows, 1, RKP/8).
-// The box lands as [RKP/8][rows][8] (16-byte rows, 8-rank chunks rows*16 bytes apart);
-// rows past T read as zero.
-int make_zpack_map(CUtensorMap* map, const void* base, int64_t B, int64_t T, int rkp, int rows);
+// 4-D bf16 map over z_pack [G*RKP/8][B][T][8]: dims (8, T, B, G*RKP/8), box (8, rows, 1,
+// RKP/8); group g's box starts at coordinate g*RKP/8 of the last dimension.  The box
+// lands as [RKP/8][rows][8] (16-byte rows, 8-rank chunks rows*16 bytes apart); rows
+// past T read as zero.
+int make_zpack_map(CUtensorMap* map, const void* base, int64_t B, int64_t T, int rkp, int rows, int G = 1);
 
-size_t zpack_bytes(int64_t B, int64_t T, int rkp);
-int z_pack_launch(const void* z, void* zp, int64_t B, int64_t T, int R, int rkp, bool has_static, cudaStream_t st);
+size_t zpack_bytes(int64_t B, int64_t T, int rkp, int G = 1);
+// z [B][T][G*R] -> z_pack [G*RKP/8][B][T][8] (static rank and zero padding per group).
+int z_pack_launch(const void* z, void* zp, int64_t B, int64_t T, int R, int rkp, bool has_static, cudaStream_t st,
+                  int G = 1);
 
 // Loads U_ext for channel block dblk into shared memory: one [128 ch x RKP] K-major
 // no-swizzle block per tap (rank R = static_w when present, zero up to RKP).  The NT

@@ -1,6 +1,6 @@
 // umma_selftest.cu -- a single-CTA tcgen05.mma check of the shared-memory
 // descriptor encodings (no-swizzle K-major and MN-major operands, arbitrary
-// SBO/LBO, row-shifted K-major B), of the 128-byte-swizzled MN-major A operand
+// SBO/LBO, row-shifted K-major A or B), of the 128-byte-swizzled MN-major A operand
 // (the layout a SWIZZLE_128B TMA load writes) and of the TMEM accumulator layout
 // for M = 64 and M = 128, as used by the lowrank tensor-core kernels.
 // Exposed through dynconv_umma_selftest() for the GPU unit tests only.
@@ -14,7 +14,7 @@ __global__ void __launch_bounds__(128) umma_selftest_kernel(const __nv_bfloat16*
                                                             const __nv_bfloat16* __restrict__ Bm,
                                                             float* __restrict__ Dout, int M, int N, int K, int Nb,
                                                             int a_major, uint32_t a_sbo, uint32_t a_lbo, int b_major,
-                                                            uint32_t b_sbo, uint32_t b_lbo, int b_off,
+                                                            uint32_t b_sbo, uint32_t b_lbo, int b_off, int a_off,
                                                             uint32_t a_bytes, uint32_t ncols) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = align_smem_1024(smem_raw);
@@ -27,7 +27,8 @@ __global__ void __launch_bounds__(128) umma_selftest_kernel(const __nv_bfloat16*
 
   const bool a_tmem = (a_major == 2);  // A staged in TMEM after the D columns
   if (!a_tmem) {
-    for (int i = tid; i < M * K; i += blockDim.x) {
+    // A has M + a_off rows; the MMA reads rows a_off .. a_off + M - 1
+    for (int i = tid; i < (M + a_off) * K; i += blockDim.x) {
       const int m = i / K, k = i % K;
       const uint32_t off = a_major == 3 ? mnmajor_sw128_off(m, k, a_lbo)
                            : a_major   ? mnmajor_off(m, k, a_sbo, a_lbo)
@@ -75,7 +76,7 @@ __global__ void __launch_bounds__(128) umma_selftest_kernel(const __nv_bfloat16*
 
   if (tid == 0) {
     const uint32_t idesc = make_idesc_bf16(M, N, a_tmem ? 0 : (a_major ? 1 : 0), b_major);
-    const uint32_t a0 = smem_u32(As), b0 = smem_u32(Bs) + (uint32_t)b_off * 16u;
+    const uint32_t a0 = smem_u32(As) + (uint32_t)a_off * 16u, b0 = smem_u32(Bs) + (uint32_t)b_off * 16u;
     for (int ks = 0; ks < K / 16; ++ks) {
       const uint64_t bd = make_smem_desc(b0 + (uint32_t)ks * 2u * b_lbo, b_lbo, b_sbo);
       if (a_tmem) {
@@ -118,13 +119,15 @@ static uint32_t span_bytes(int major, int mn_extent, int k_extent, uint32_t sbo,
 }
 
 int umma_selftest_launch(const void* A, const void* B, float* D, int M, int N, int K, int Nb, int a_major, int a_sbo,
-                         int a_lbo, int b_major, int b_sbo, int b_lbo, int b_off, cudaStream_t st) {
+                         int a_lbo, int b_major, int b_sbo, int b_lbo, int b_off, int a_off, cudaStream_t st) {
   if (!(M == 64 || M == 128)) return set_error(DYNCONV_ERR_SHAPE, "selftest: M must be 64 or 128");
   if (N < 16 || N > 256 || N % 16 != 0) return set_error(DYNCONV_ERR_SHAPE, "selftest: N in 16..256, multiple of 16");
   if (K < 16 || K % 16 != 0) return set_error(DYNCONV_ERR_SHAPE, "selftest: K multiple of 16");
   if (Nb < N + b_off) return set_error(DYNCONV_ERR_SHAPE, "selftest: Nb < N + b_row_offset");
   if (b_off != 0 && (b_major != 0 || b_sbo != 128))
     return set_error(DYNCONV_ERR_SHAPE, "selftest: row offset needs K-major B with SBO = 128");
+  if (a_off < 0 || b_off < 0 || a_off > 64 || (a_off != 0 && (a_major != 0 || a_sbo != 128)))
+    return set_error(DYNCONV_ERR_SHAPE, "selftest: A row offset (0..64) needs K-major A with SBO = 128");
   if ((a_sbo | a_lbo | b_sbo | b_lbo) & 15) return set_error(DYNCONV_ERR_ALIGN, "selftest: strides must be 16-byte multiples");
   if (a_major == 2 && (M != 128 || N + K / 2 > 256))
     return set_error(DYNCONV_ERR_SHAPE, "selftest: A in TMEM needs M = 128 and N + K/2 <= 256");
@@ -132,7 +135,7 @@ int umma_selftest_launch(const void* A, const void* B, float* D, int M, int N, i
     return set_error(DYNCONV_ERR_SHAPE, "selftest: swizzled A needs SBO = 1024 and LBO a multiple of 1024 past its rows");
   const uint32_t abytes = a_major == 2   ? 128u
                           : a_major == 3 ? (uint32_t)((M + 63) / 64) * (uint32_t)a_lbo
-                                         : span_bytes(a_major, M, K, (uint32_t)a_sbo, (uint32_t)a_lbo);
+                                         : span_bytes(a_major, M + a_off, K, (uint32_t)a_sbo, (uint32_t)a_lbo);
   const uint32_t bbytes = span_bytes(b_major, Nb, K, (uint32_t)b_sbo, (uint32_t)b_lbo);
   const uint32_t smem = (abytes + 1023u) / 1024u * 1024u + bbytes;
   if (smem > 200 * 1024) return set_error(DYNCONV_ERR_SHAPE, "selftest: operands need %u bytes of smem", smem);
@@ -144,7 +147,7 @@ int umma_selftest_launch(const void* A, const void* B, float* D, int M, int N, i
   if (e != cudaSuccess) return cuda_status(e, "cudaFuncSetAttribute(umma_selftest)");
   umma_selftest_kernel<<<1, 128, smem_alloc, st>>>((const __nv_bfloat16*)A, (const __nv_bfloat16*)B, D, M, N, K, Nb,
                                                    a_major, (uint32_t)a_sbo, (uint32_t)a_lbo, b_major, (uint32_t)b_sbo,
-                                                   (uint32_t)b_lbo, b_off, abytes, ncols);
+                                                   (uint32_t)b_lbo, b_off, a_off, abytes, ncols);
   DYNCONV_CHECK_LAUNCH("umma_selftest_kernel");
   return DYNCONV_OK;
 }

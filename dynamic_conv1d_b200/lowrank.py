@@ -145,3 +145,138 @@ def lowrank_dynamic_convolution(
         assert static_w.dtype == z.dtype == U.dtype
         assert static_w.shape == (U.shape[-1] // x.shape[-1], x.shape[-1])
     return _LowrankDynamicConvolutionFn.apply(x, z, U, static_w, residual)
+
+
+class _LowrankGroupedFn(torch.autograd.Function):
+    """G lowrank convolutions in one launch per direction (``dynconv_lr_fwd_grouped``
+    / ``dynconv_lr_bwd_grouped``): x [B,T,G*D], z [B,T,G*R], U [G,R,W*D],
+    static_w [G,W,D].  bf16 tensor-core path only; ``lowrank_dynamic_convolution_grouped``
+    checks the envelope and otherwise runs the groups one by one."""
+
+    @staticmethod
+    @_lib.on_device
+    def forward(ctx, x, z, U, static_w, residual):
+        B, T, Dt = x.shape
+        G, R = U.shape[0], U.shape[1]
+        D = Dt // G
+        W = U.shape[-1] // D
+        lib = _lib.load()
+        code = _lib.dtype_code(x.dtype)
+        y = torch.empty_like(x)
+        has_static = static_w is not None
+        nbytes = lib.dynconv_lr_fwd_grouped_workspace_bytes(B, T, D, R, W, G, code, int(has_static))
+        ws = torch.empty(max(int(nbytes), 1), device=x.device, dtype=torch.uint8)
+        _lib.check(
+            lib.dynconv_lr_fwd_grouped(
+                _lib.ptr(x), _lib.ptr(z), _lib.ptr(U), _lib.ptr(static_w), _lib.ptr(y),
+                _lib.ptr(ws), ws.numel(),
+                B, T, D, R, W, G, code, int(bool(residual)), _lib.stream_of(x),
+            )
+        )
+        _lib.after_call(y)
+        ctx.save_for_backward(x, z, U, static_w)
+        ctx.residual = bool(residual)
+        ctx.group = current_group()
+        return y
+
+    @staticmethod
+    @_lib.on_device
+    def backward(ctx, dy):
+        dy = dy.contiguous()
+        x, z, U, static_w = ctx.saved_tensors
+        B, T, Dt = x.shape
+        G, R = U.shape[0], U.shape[1]
+        D = Dt // G
+        W = U.shape[-1] // D
+        has_static = static_w is not None
+        Rk = R + (1 if has_static else 0)
+        lib = _lib.load()
+        code = _lib.dtype_code(x.dtype)
+        if dy.dtype != x.dtype:
+            dy = dy.to(x.dtype)
+        dx = torch.empty_like(x)
+        dz = torch.empty_like(z)
+        dU_f32 = torch.empty((G, Rk, W * D), device=x.device, dtype=torch.float32)
+        nbytes = lib.dynconv_lr_bwd_grouped_workspace_bytes(B, T, D, R, W, G, code, int(has_static))
+        ws = torch.empty(max(int(nbytes), 1), device=x.device, dtype=torch.uint8)
+        reduce_first = ctx.group is not None
+        dU = None if reduce_first else torch.empty_like(U)
+        dsw = None if (reduce_first or not has_static) else torch.empty_like(static_w)
+        stream = _lib.stream_of(x)
+        _lib.check(
+            lib.dynconv_lr_bwd_grouped(
+                _lib.ptr(x), _lib.ptr(z), _lib.ptr(U), _lib.ptr(static_w), _lib.ptr(dy),
+                _lib.ptr(dx), _lib.ptr(dz), _lib.ptr(dU), _lib.ptr(dsw), _lib.ptr(dU_f32),
+                _lib.ptr(ws), ws.numel(),
+                B, T, D, R, W, G, code, int(ctx.residual), stream,
+            )
+        )
+        if reduce_first:
+            # one all-reduce for all G groups' dU and dstatic_w rows
+            allreduce_shared_grad(dU_f32, ctx.group)
+            g = torch.empty((G, Rk, W * D), device=x.device, dtype=x.dtype)
+            _lib.check(lib.dynconv_cast_f32(_lib.ptr(dU_f32), _lib.ptr(g), G * Rk * W * D, code, stream))
+            dU = g[:, :R]
+            if has_static:
+                dsw = g[:, R].view(G, W, D)
+        _lib.after_call(dx)
+        return dx, dz, dU, dsw, None
+
+
+def grouped_supported(x: torch.Tensor, D: int, R: int, W: int, G: int, has_static: bool) -> bool:
+    """Whether the one-launch grouped kernels take this call (bf16, W <= 4,
+    R_kernel <= 32, D % 128 == 0, G*D/128 CTAs co-resident, 16-byte aligned)."""
+    Rk = R + (1 if has_static else 0)
+    if x.dtype != torch.bfloat16 or not (1 <= W <= 4) or Rk > 32 or D % 128 != 0:
+        return False
+    props = torch.cuda.get_device_properties(x.device)
+    return G * D // 128 <= props.multi_processor_count
+
+
+def lowrank_dynamic_convolution_grouped(
+    x: torch.Tensor,
+    z: torch.Tensor,
+    U: torch.Tensor,
+    static_w: torch.Tensor | None = None,
+    residual: bool = False,
+) -> torch.Tensor:
+    """G low-rank dynamic convolutions side by side -- e.g. the query, key and value
+    convolutions of one attention layer (reference README.md:86-105) -- computed
+    by one forward and one backward kernel launch.
+
+    Args:
+        x:        [B, T, G*D]; group g's input is x[..., g*D:(g+1)*D] (the layout of a
+                  fused QKV projection's output, read in place).
+        z:        [B, T, G*R]; group g's mixing coefficients are z[..., g*R:(g+1)*R].
+        U:        [G, R, W*D], one second projection per group.
+        static_w: [G, W, D] optional static filters (one extra rank per group).
+        residual: add x to the output.
+
+    Returns:
+        y [B, T, G*D] with y[..., g*D:(g+1)*D] =
+        lowrank_dynamic_convolution(x_g, z_g, U[g], static_w[g], residual).
+
+    Under ``data_parallel()`` the backward all-reduces one [G, R_kernel, W*D]
+    buffer.  Outside the grouped kernels' envelope (see ``grouped_supported``) the
+    groups run one by one through ``lowrank_dynamic_convolution``.
+    """
+    assert x.is_cuda and x.is_contiguous() and z.is_contiguous() and U.is_contiguous()
+    G, R = U.shape[0], U.shape[1]
+    B, T, Dt = x.shape
+    assert Dt % G == 0 and z.shape == (B, T, G * R), "x must be [B,T,G*D] and z [B,T,G*R]"
+    D = Dt // G
+    W = U.shape[-1] // D
+    R_kernel = R + 1 if static_w is not None else R
+    assert R_kernel & (R_kernel - 1) == 0, "rank R must be a power of 2. If static_w is set R+1 must be a power of 2."
+    if static_w is not None:
+        assert static_w.is_contiguous() and static_w.shape == (G, W, D)
+        assert static_w.dtype == z.dtype == U.dtype
+    if G > 1 and z.dtype == U.dtype == x.dtype and grouped_supported(x, D, R, W, G, static_w is not None):
+        return _LowrankGroupedFn.apply(x, z, U, static_w, residual)
+    outs = [
+        lowrank_dynamic_convolution(
+            x[..., g * D:(g + 1) * D].contiguous(), z[..., g * R:(g + 1) * R].contiguous(), U[g],
+            None if static_w is None else static_w[g], residual)
+        for g in range(G)
+    ]
+    return torch.cat(outs, dim=-1)

@@ -8,10 +8,10 @@ the pre-norm input, ``proj_out`` is U (zeros, [R, W*d_model]), and
 ``proj_out_bias`` is static_w ([W, d_model], uniform in +-1/sqrt(W)), folded into
 the kernels as rank R -- so R+1 must be a power of two.
 
-``QKVLowRankDynamicShortConvolution`` holds the three modules' parameters and
+``QKVLowRankDynamicShortConvolution`` holds the three modules' parameters,
 computes the three z projections as one GEMM (the three proj_in weights stacked,
-one read of the pre-norm activations instead of three) before the three
-convolutions.
+one read of the pre-norm activations instead of three) and the three
+convolutions as one grouped kernel launch per direction.
 
 proj_in is an ordinary GEMM (cuBLAS through ``torch.nn.functional.linear``): z
 needs a dot product over all d_model channels for each token, while a
@@ -24,7 +24,7 @@ import math
 import torch
 from torch import nn
 
-from .lowrank import lowrank_dynamic_convolution
+from .lowrank import lowrank_dynamic_convolution, lowrank_dynamic_convolution_grouped
 
 
 def _check_rank(R: int) -> None:
@@ -63,8 +63,16 @@ class QKVLowRankDynamicShortConvolution(nn.Module):
     """The query, key and value convolutions of one attention layer.
 
     Parameters are those of three ``LowRankDynamicShortConvolution`` modules
-    (``q``, ``k``, ``v``); forward(q, k, v, pre_z) returns the three convolved
-    tensors.  The three proj_in GEMMs run as one over the stacked weights.
+    (``q``, ``k``, ``v``).  The three proj_in GEMMs run as one over the stacked
+    weights, and the three convolutions as one grouped launch per direction
+    (``lowrank_dynamic_convolution_grouped``), with one all-reduce of the stacked
+    dU / static_w gradients under ``data_parallel()``.
+
+    ``forward_fused(qkv, pre_z)`` takes the fused projection output [B, T, 3*d_model]
+    as it comes out of the QKV GEMM and returns the three results in the same
+    layout, with no split or copy.  ``forward(q, k, v, pre_z)`` takes the three
+    tensors (concatenated once, as the reference's ``.contiguous()`` calls copy
+    them) and returns three [B, T, d_model] views.
     """
 
     def __init__(self, d_model: int, R: int, W: int):
@@ -73,13 +81,14 @@ class QKVLowRankDynamicShortConvolution(nn.Module):
         self.k = LowRankDynamicShortConvolution(d_model, R, W)
         self.v = LowRankDynamicShortConvolution(d_model, R, W)
 
-    def forward(self, q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, pre_z: torch.Tensor):
+    def forward_fused(self, qkv: torch.Tensor, pre_z: torch.Tensor) -> torch.Tensor:
         mods = (self.q, self.k, self.v)
-        R = self.q.R
         w_in = torch.cat([m.proj_in.weight for m in mods], dim=0)  # [3R, d_model]
         z_all = torch.nn.functional.linear(pre_z, w_in)  # [B, T, 3R]
-        outs = []
-        for i, (m, t) in enumerate(zip(mods, (q, k, v))):
-            z = z_all[..., i * R:(i + 1) * R].contiguous()
-            outs.append(lowrank_dynamic_convolution(t.contiguous(), z, m.proj_out, m.proj_out_bias, residual=True))
-        return tuple(outs)
+        U = torch.stack([m.proj_out for m in mods])  # [3, R, W*d_model]
+        sw = torch.stack([m.proj_out_bias for m in mods])  # [3, W, d_model]
+        return lowrank_dynamic_convolution_grouped(qkv.contiguous(), z_all.contiguous(), U, sw, residual=True)
+
+    def forward(self, q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, pre_z: torch.Tensor):
+        y = self.forward_fused(torch.cat([q, k, v], dim=-1), pre_z)
+        return y.split(self.q.d_model, dim=-1)

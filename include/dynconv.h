@@ -162,6 +162,39 @@ int dynconv_lr_bwd(const void* x, const void* z, const void* U, const void* stat
                    int64_t B, int64_t T, int64_t D, int64_t R, int64_t W,
                    int dtype, int residual, void* stream);
 
+/* ------------------------------------------------------ grouped (Q/K/V) lowrank */
+
+/* G low-rank convolutions that share B, T, D, R, W -- the query, key and value
+ * convolutions of one attention layer (reference README.md:86-105, three
+ * LowRankDynamicShortConvolution modules) -- in one launch of each kernel.  No
+ * reference counterpart as one call: it replaces G calls of dynconv_lr_fwd /
+ * dynconv_lr_bwd, with the same results per group.
+ *   x, y, dy, dx : [B, T, G*D]  group g owns channels [g*D, (g+1)*D) of each row --
+ *                  the layout of a fused QKV projection's output, so q, k and v
+ *                  are read in place, with no split or copy
+ *   z, dz        : [B, T, G*R]  group g's z in columns [g*R, (g+1)*R)
+ *   U, dU        : [G, R, W*D]
+ *   static_w, dstatic_w : [G, W, D] (optional, as for the single op)
+ *   dU_f32       : [G, R_kernel, W*D], group g's rows as dynconv_lr_bwd's dU_f32
+ * With G > 1 the call needs the tensor-core path: bf16, W <= 4, R_kernel <= 64
+ * (forward) / <= 32 (backward), D % 128 == 0, G*D/128 <= the SM count (backward),
+ * 16-byte aligned tensors; anything else returns DYNCONV_ERR_UNSUPPORTED (call
+ * the single op per group).  G = 1 is exactly dynconv_lr_fwd / dynconv_lr_bwd.
+ * G in 1..16. */
+size_t dynconv_lr_fwd_grouped_workspace_bytes(int64_t B, int64_t T, int64_t D, int64_t R, int64_t W, int64_t G,
+                                              int dtype, int has_static);
+int dynconv_lr_fwd_grouped(const void* x, const void* z, const void* U, const void* static_w, void* y,
+                           void* workspace, size_t workspace_bytes,
+                           int64_t B, int64_t T, int64_t D, int64_t R, int64_t W, int64_t G,
+                           int dtype, int residual, void* stream);
+size_t dynconv_lr_bwd_grouped_workspace_bytes(int64_t B, int64_t T, int64_t D, int64_t R, int64_t W, int64_t G,
+                                              int dtype, int has_static);
+int dynconv_lr_bwd_grouped(const void* x, const void* z, const void* U, const void* static_w, const void* dy,
+                           void* dx, void* dz, void* dU, void* dstatic_w, float* dU_f32,
+                           void* workspace, size_t workspace_bytes,
+                           int64_t B, int64_t T, int64_t D, int64_t R, int64_t W, int64_t G,
+                           int dtype, int residual, void* stream);
+
 /* dst[i] = (dtype) src[i], i < n, round-to-nearest-even.  Used after the
  * data-parallel all-reduce of the float32 shared-gradient buffers (replaces
  * dU_fp32.to(U.dtype), lowrank.py:294, and dstatic_accum.to(...), headwise.py:305). */
@@ -176,12 +209,13 @@ int dynconv_cast_f32(const float* src, void* dst, int64_t n, int dtype, void* st
  * row-major (Nb >= N + b_row_offset); D: [M][N] float32 = A @ B[:, off:off+N].
  * a_major/b_major: 0 = K-major, 1 = MN-major (a_major 2: A staged K-major in
  * tensor memory, M = 128); *_sbo/*_lbo: byte strides of the staged layout;
- * b_row_offset shifts a K-major B by whole rows (16 B each). */
+ * b_row_offset shifts a K-major B by whole rows (16 B each); a_row_offset does
+ * the same for a K-major A given with M + a_row_offset rows (D = A[off:off+M] @ B). */
 int dynconv_umma_selftest(const void* A, const void* B, float* D,
                           int M, int N, int K, int Nb,
                           int a_major, int a_sbo, int a_lbo,
                           int b_major, int b_sbo, int b_lbo, int b_row_offset,
-                          void* stream);
+                          int a_row_offset, void* stream);
 
 /* Test hook for the fault-containment path (no reference counterpart): launches one
  * CTA that waits on an mbarrier no thread ever arrives on, through the kernels'

@@ -26,7 +26,8 @@ CHILD = textwrap.dedent(
     import sys, datetime
     import torch, torch.distributed as dist
     sys.path.insert(0, {root!r})
-    from dynamic_conv1d_b200 import data_parallel, headwise_dynamic_convolution, lowrank_dynamic_convolution
+    from dynamic_conv1d_b200 import (data_parallel, headwise_dynamic_convolution, lowrank_dynamic_convolution,
+                                     lowrank_dynamic_convolution_grouped)
     dist.init_process_group("nccl", init_method="tcp://127.0.0.1:{port}", rank=0, world_size=1,
                             timeout=datetime.timedelta(seconds=60), device_id=torch.device("cuda", 0))
     dev = torch.device("cuda", 0)
@@ -53,10 +54,14 @@ CHILD = textwrap.dedent(
         "lowrank_static": (lowrank_dynamic_convolution, [x, rnd(B, T, 15), rnd(15, W * D, scale=0.25), rnd(W, D, scale=0.3)]),
         "lowrank_nostatic": (lowrank_dynamic_convolution, [x, rnd(B, T, 16), rnd(16, W * D, scale=0.25)]),
         "headwise_hs32": (headwise_dynamic_convolution, [x, rnd(B, T, D // 32, W, scale=0.3), rnd(W, D, scale=0.3)]),
+        "lowrank_grouped": (lowrank_dynamic_convolution_grouped,
+                            [rnd(B, T, 3 * D), rnd(B, T, 3 * 15), rnd(3, 15, W * D, scale=0.25), rnd(3, W, D, scale=0.3)]),
     }}
+    dy3 = rnd(B, T, 3 * D)
     for name, (fn, leaves) in cases.items():
-        ref = grads(fn, leaves, dy, dp=False)
-        got = grads(fn, leaves, dy, dp=True)
+        d = dy3 if name == "lowrank_grouped" else dy
+        ref = grads(fn, leaves, d, dp=False)
+        got = grads(fn, leaves, d, dp=True)
         for i, (a, b) in enumerate(zip(ref, got)):
             assert a.shape == b.shape and a.dtype == b.dtype, (name, i, a.shape, b.shape, a.dtype, b.dtype)
             assert torch.equal(a, b), (name, i, (a.float() - b.float()).abs().max().item())
@@ -76,7 +81,7 @@ def test_data_parallel_backward_matches_single_process(cuda_device):
     code = CHILD.format(root=ROOT, port=_free_port())
     r = subprocess.run([sys.executable, "-c", code], capture_output=True, text=True, timeout=240)
     assert r.returncode == 0, r.stdout[-2000:] + r.stderr[-4000:]
-    assert r.stdout.count("ok ") == 3, r.stdout
+    assert r.stdout.count("ok ") == 4, r.stdout
 
 
 THREAD_CHILD = textwrap.dedent(

@@ -47,24 +47,36 @@ CASES = {
     "sw128_transpose": (128, 16, 16, 16, 3, 1024, 2048, 0, 128, 256, 0),
     "sw128_K32": (128, 32, 32, 32, 3, 1024, 4096, 0, 128, 512, 0),
     "sw128_M64": (64, 16, 16, 16, 3, 1024, 2048, 0, 128, 256, 0),
+    # time-major backward (M = 128 timesteps): weight MMA, A = z rows t+w (K-major, rows
+    # 16 B apart, 8-rank chunks 136 rows apart), B = U tap w (MN-major, N = 32 channels)
+    "tm_w_R16": (128, 32, 16, 32, 0, 128, 136 * 16, 1, 256, 128, 0, 0),
+    "tm_w_R16_shift3": (128, 32, 16, 32, 0, 128, 136 * 16, 1, 256, 128, 0, 3),
+    "tm_w_R32_shift2": (128, 32, 32, 32, 0, 128, 136 * 16, 1, 512, 128, 0, 2),
+    # dz MMA: A = P [t][(tap, ch)] K-major (8-step groups 2048 B apart), B = U K-major
+    "tm_dz_R16": (128, 16, 32, 16, 0, 2048, 128, 0, 128, 256, 0),
+    "tm_dz_R32": (128, 32, 32, 32, 0, 2048, 128, 0, 128, 512, 0),
+    # dU MMA: A = the same P buffer read MN-major (M = 4 taps x 32 channels), B = z MN-major
+    "tm_dU_R16": (128, 16, 128, 16, 1, 128, 2048, 1, 136 * 16, 128, 0),
+    "tm_dU_R32": (128, 32, 128, 32, 1, 128, 2048, 1, 136 * 16, 128, 0),
 }
 
 
 @pytest.mark.parametrize("name", list(CASES))
 def test_umma_layout(name, cuda_device):
-    M, N, K, Nb, am, asbo, albo, bm, bsbo, blbo, off = CASES[name]
+    M, N, K, Nb, am, asbo, albo, bm, bsbo, blbo, off, *rest = CASES[name]
+    a_off = rest[0] if rest else 0
     g = torch.Generator(device="cuda").manual_seed(zlib.crc32(name.encode()))
-    A = torch.randn(M, K, device="cuda", generator=g).to(torch.bfloat16)
+    A = torch.randn(M + a_off, K, device="cuda", generator=g).to(torch.bfloat16)
     B = torch.randn(K, Nb, device="cuda", generator=g).to(torch.bfloat16)
     D = torch.full((M, N), float("nan"), device="cuda", dtype=torch.float32)
     lib = _lib.load()
     st = lib.dynconv_umma_selftest(
         ctypes.c_void_p(A.data_ptr()), ctypes.c_void_p(B.data_ptr()), ctypes.c_void_p(D.data_ptr()),
-        M, N, K, Nb, am, asbo, albo, bm, bsbo, blbo, off, _lib.stream_of(A),
+        M, N, K, Nb, am, asbo, albo, bm, bsbo, blbo, off, a_off, _lib.stream_of(A),
     )
     _lib.check(st)
     _lib.check_device(A)
-    ref = A.float() @ B.float()[:, off:off + N]
+    ref = A.float()[a_off:a_off + M] @ B.float()[:, off:off + N]
     torch.testing.assert_close(D, ref, atol=1e-3, rtol=1e-3)
 
 
@@ -78,7 +90,7 @@ def test_transpose_is_exact(cuda_device):
     lib = _lib.load()
     _lib.check(lib.dynconv_umma_selftest(
         ctypes.c_void_p(A.data_ptr()), ctypes.c_void_p(B.data_ptr()), ctypes.c_void_p(D.data_ptr()),
-        M, N, K, K, 3, 1024, 2048, 0, 128, 256, 0, _lib.stream_of(A),
+        M, N, K, K, 3, 1024, 2048, 0, 128, 256, 0, 0, _lib.stream_of(A),
     ))
     _lib.check_device(A)
     assert torch.equal(D, A.float())
