@@ -422,6 +422,7 @@ class DeviceStep:
             torch.cuda.synchronize()
             wall = time.perf_counter() - wall0
             launches = lib.dynconv_launch_count() - launches0
+            _lib.check_device(self.leaves[0])  # raises if a kernel gave up a bounded wait
             # The timed region is a few milliseconds, shorter than the 200 ms sampling
             # period: keep the same step running (untimed) until the sampler has seen
             # at least 3 samples under this load.  Every replay holds the data-parallel
@@ -758,6 +759,7 @@ def kernel_roofline(args, wl, leaves, dy, fn, flush, dev, workload=None) -> dict
     n = max(10, args.steps)
     t_fwd = timed(fwd, n)
     t_bwd = timed(bwd, n)
+    _lib.check_device(x)
     fwd_b, bwd_b = algorithmic_bytes(wl)
     peak, src = _peaks()
     ach = bwd_b / (t_bwd / 1e3) / 1e9

@@ -10,6 +10,7 @@
 #include <string.h>
 
 #include "common.cuh"
+#include "lowrank_tc.cuh"
 
 namespace dynconv {
 
@@ -84,6 +85,8 @@ int sm_count() {
 
 unsigned int lr_tc_error_word();
 unsigned int lr_bwd_error_word();
+unsigned int lr_bwd_tm_error_word();
+unsigned int lr_fwd_tm_error_word();
 unsigned int hw_tma_error_word();
 bool hw_tma_supported(int64_t D, int64_t H, int W, int log2hs, int dtype, const void* const* ptrs, int nptrs);
 int hw_tma_partial_rows(int64_t B, int64_t T, int64_t D, int log2hs);
@@ -120,6 +123,11 @@ int lr_tc_fwd_launch(const void* x, const void* z, const void* U, const void* sw
 int lr_tc_bwd_launch(const void* x, const void* z, const void* U, const void* sw, const void* dy, void* dx, void* dz,
                      float* dU_f32, void* dU, void* dsw, void* ws, size_t ws_bytes, int64_t B, int64_t T, int64_t D,
                      int G, int R, int Rk, int W, int residual, cudaStream_t st);
+int lr_tm_bwd_launch(const void* x, const void* z, const void* U, const void* sw, const void* dy, void* dx, void* dz,
+                     float* dU_f32, void* dU, void* dsw, void* ws, size_t ws_bytes, int64_t B, int64_t T, int64_t D,
+                     int G, int R, int Rk, int W, int residual, const lrtc::DpPeers* peers, cudaStream_t st);
+bool comm_peers(const void* comm, lrtc::DpPeers* out);
+int comm_device(const void* comm);
 
 namespace {
 
@@ -179,11 +187,13 @@ int dynconv_check_device(void* stream) {
   cudaError_t e = cudaStreamSynchronize(st);
   if (e != cudaSuccess) return cuda_status(e, "cudaStreamSynchronize");
   // every word is read (and so cleared) before the first non-zero one is reported
-  const unsigned int words[4] = {lr_tc_error_word(), lr_bwd_error_word(), selftest_error_word(), hw_tma_error_word()};
-  static const char* const kFile[4] = {"lowrank forward", "lowrank backward", "self-test", "headwise"};
+  const unsigned int words[6] = {lr_tc_error_word(), lr_fwd_tm_error_word(), lr_bwd_error_word(),
+                                 lr_bwd_tm_error_word(), selftest_error_word(), hw_tma_error_word()};
+  static const char* const kFile[6] = {"lowrank forward", "lowrank forward", "lowrank backward", "lowrank backward",
+                                       "self-test", "headwise"};
   for (unsigned int v : words)
     if (v == 0xFFFFFFFFu) return set_error(DYNCONV_ERR_CUDA, "could not read the device error word");
-  for (int i = 0; i < 4; ++i)
+  for (int i = 0; i < 6; ++i)
     if (words[i] != 0)
       return set_error(DYNCONV_ERR_TIMEOUT, "a device-side bounded wait gave up (%s kernel, site %u)", kFile[i],
                        words[i]);
@@ -395,6 +405,36 @@ int dynconv_lr_bwd_grouped(const void* x, const void* z, const void* U, const vo
   const int P = (int)lr_simple_partial_rows(B, T);
   if ((s = reduce_partials_launch(part, P, nacc, dU_f32, nullptr, dtype, st))) return s;
   return cast_grouped(dU_f32, dU, has_static ? dstatic_w : nullptr, 1, R, Rk, W, D, dtype, st);
+}
+
+int dynconv_lr_bwd_grouped_dp(const void* x, const void* z, const void* U, const void* static_w, const void* dy,
+                              void* dx, void* dz, void* dU, void* dstatic_w, float* dU_f32, void* workspace,
+                              size_t workspace_bytes, int64_t B, int64_t T, int64_t D, int64_t R, int64_t W, int64_t G,
+                              int dtype, int residual, void* comm, void* stream) {
+  int s;
+  if ((s = lr_checks(B, T, D, R, W, dtype))) return s;
+  if ((s = check_groups(G))) return s;
+  const bool has_static = static_w != nullptr;
+  const int Rk = (int)R + (has_static ? 1 : 0);
+  if (!dU_f32) return set_error(DYNCONV_ERR_ARGUMENT, "lr_bwd_dp: dU_f32 required");
+  if (!x || !z || !U || !dy || !dx || !dz) return set_error(DYNCONV_ERR_ARGUMENT, "lr_bwd_dp: null tensor");
+  lrtc::DpPeers peers;
+  if (!comm_peers(comm, &peers)) return set_error(DYNCONV_ERR_ARGUMENT, "lr_bwd_dp: communicator missing or not connected");
+  int dev = -1;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev != comm_device(comm))
+    return set_error(DYNCONV_ERR_ARGUMENT, "lr_bwd_dp: the communicator belongs to device %d, current is %d",
+                     comm_device(comm), dev);
+  const void* ptrs[] = {x, z, U, static_w, dy, dx, dz};
+  if (B * T == 0 || !lr_tc_bwd_supported(D, Rk, (int)W, dtype, ptrs, 7, (int)G))
+    return set_error(DYNCONV_ERR_UNSUPPORTED,
+                     "lr_bwd_dp: the fused data-parallel backward needs the tensor-core path (bf16, W <= 4, "
+                     "R_kernel <= 32, B*T > 0, 16-byte aligned tensors); all-reduce dU_f32 of dynconv_lr_bwd_grouped "
+                     "instead");
+  const size_t need = dynconv_lr_bwd_grouped_workspace_bytes(B, T, D, R, W, G, dtype, has_static);
+  if (!workspace || workspace_bytes < need)
+    return set_error(DYNCONV_ERR_WORKSPACE, "lr_bwd_dp: workspace %zu < %zu bytes", workspace_bytes, need);
+  return lr_tm_bwd_launch(x, z, U, static_w, dy, dx, dz, dU_f32, dU, dstatic_w, workspace, workspace_bytes, B, T, D,
+                          (int)G, (int)R, Rk, (int)W, residual, &peers, (cudaStream_t)stream);
 }
 
 int dynconv_lr_bwd(const void* x, const void* z, const void* U, const void* static_w, const void* dy, void* dx,

@@ -718,8 +718,8 @@ int launch_bwd(const void* x, const void* z, const void* U, const void* sw, cons
     if ((s = make_btd4_map(&dymap, dy, B, T, Dt, kQ))) return s;
     if ((s = make_btd4_map(&xmap, x, B, T, Dt, kQ))) return s;
   } else {
-    if ((s = make_btd_map(&dymap, dy, B, T, Dt, 64, kQ, true))) return s;
-    if ((s = make_btd_map(&xmap, x, B, T, Dt, 64, kQ, true))) return s;
+    if ((s = make_btd_map(&dymap, dy, B, T, Dt, 64, kQ, 128))) return s;
+    if ((s = make_btd_map(&xmap, x, B, T, Dt, 64, kQ, 128))) return s;
   }
   if ((s = make_zpack_map(&zmap, ws.zp, B, T, RKP, kZRows, G))) return s;
   if ((s = z_pack_launch(z, ws.zp, B, T, R, RKP, sw != nullptr, st, G))) return s;
@@ -784,14 +784,26 @@ bool lr_tc_bwd_supported(int64_t D, int Rk, int W, int dtype, const void* const*
   return encode_fn() != nullptr || nptrs == 0;
 }
 
+size_t lr_tm_bwd_workspace(int64_t B, int64_t T, int64_t D, int Rk, int W, int G);
+int lr_tm_bwd_launch(const void* x, const void* z, const void* U, const void* sw, const void* dy, void* dx, void* dz,
+                     float* dU_f32, void* dU, void* dsw, void* ws, size_t ws_bytes, int64_t B, int64_t T, int64_t D,
+                     int G, int R, int Rk, int W, int residual, const DpPeers* peers, cudaStream_t st);
+
 size_t lr_tc_bwd_workspace(int64_t B, int64_t T, int64_t D, int Rk, int W, int G) {
-  return bwd_workspace(nullptr, B, T, D, Rk, W, G).bytes;
+  return lr_tm_bwd_workspace(B, T, D, Rk, W, G);
 }
 
 int lr_tc_bwd_launch(const void* x, const void* z, const void* U, const void* sw, const void* dy, void* dx, void* dz,
                      float* dU_f32, void* dU, void* dsw, void* ws, size_t ws_bytes, int64_t B, int64_t T, int64_t D,
                      int G, int R, int Rk, int W, int residual, cudaStream_t st) {
-  if (ws_bytes < lr_tc_bwd_workspace(B, T, D, Rk, W, G))
+  return lr_tm_bwd_launch(x, z, U, sw, dy, dx, dz, dU_f32, dU, dsw, ws, ws_bytes, B, T, D, G, R, Rk, W, residual,
+                          nullptr, st);
+}
+
+int lr_tc_bwd_launch_quarters(const void* x, const void* z, const void* U, const void* sw, const void* dy, void* dx, void* dz,
+                     float* dU_f32, void* dU, void* dsw, void* ws, size_t ws_bytes, int64_t B, int64_t T, int64_t D,
+                     int G, int R, int Rk, int W, int residual, cudaStream_t st) {
+  if (ws_bytes < bwd_workspace(nullptr, B, T, D, Rk, W, G).bytes)
     return set_error(DYNCONV_ERR_WORKSPACE, "lr_bwd (tensor core): workspace too small");
   if (Rk <= 16)
     return launch_bwd_w<16>(W, x, z, U, sw, dy, dx, dz, dU_f32, dU, dsw, ws, B, T, D, G, R, Rk, residual, st);

@@ -51,16 +51,22 @@ EncodeTiledFn encode_fn() {
 }
 
 int make_btd_map(CUtensorMap* map, const void* base, int64_t B, int64_t T, int64_t D, int box_d, int box_t,
-                 bool swizzle128) {
+                 int swizzle_bytes) {
   EncodeTiledFn fn = encode_fn();
   if (!fn) return set_error(DYNCONV_ERR_CUDA, "cuTensorMapEncodeTiled unavailable");
+  if (swizzle_bytes != 0 && box_d * 2 != swizzle_bytes)
+    return set_error(DYNCONV_ERR_SHAPE, "swizzled map: box of %d channels != %d bytes", box_d, swizzle_bytes);
   if (int s = ensure_context()) return s;
   cuuint64_t dims[3] = {(cuuint64_t)D, (cuuint64_t)T, (cuuint64_t)B};
   cuuint64_t strides[2] = {(cuuint64_t)D * 2, (cuuint64_t)T * D * 2};
   cuuint32_t box[3] = {(cuuint32_t)box_d, (cuuint32_t)box_t, 1};
   cuuint32_t estr[3] = {1, 1, 1};
   CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<void*>(base), dims, strides, box, estr,
-                  CU_TENSOR_MAP_INTERLEAVE_NONE, swizzle128 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_NONE,
+                  CU_TENSOR_MAP_INTERLEAVE_NONE,
+                  swizzle_bytes == 128  ? CU_TENSOR_MAP_SWIZZLE_128B
+                  : swizzle_bytes == 64 ? CU_TENSOR_MAP_SWIZZLE_64B
+                  : swizzle_bytes == 32 ? CU_TENSOR_MAP_SWIZZLE_32B
+                                        : CU_TENSOR_MAP_SWIZZLE_NONE,
                   CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (r != CUDA_SUCCESS) return set_error(DYNCONV_ERR_CUDA, "cuTensorMapEncodeTiled failed (%d)", (int)r);
   return DYNCONV_OK;
@@ -393,8 +399,19 @@ size_t lr_tc_fwd_workspace(int64_t B, int64_t T, int Rk, int G) {
   return zpack_bytes(B, T, (Rk + 15) / 16 * 16, G);
 }
 
+int lr_tm_fwd_launch(const void* x, const void* z, const void* U, const void* sw, void* y, void* ws, int64_t B,
+                     int64_t T, int64_t D, int G, int R, int Rk, int W, int residual, cudaStream_t st);
+
 int lr_tc_fwd_launch(const void* x, const void* z, const void* U, const void* sw, void* y, void* ws, size_t ws_bytes,
                      int64_t B, int64_t T, int64_t D, int G, int R, int Rk, int W, int residual, cudaStream_t st) {
+  if (!ws || ws_bytes < lr_tc_fwd_workspace(B, T, Rk, G))
+    return set_error(DYNCONV_ERR_WORKSPACE, "lr_fwd (tensor core): workspace too small");
+  return lr_tm_fwd_launch(x, z, U, sw, y, ws, B, T, D, G, R, Rk, W, residual, st);
+}
+
+int lr_tc_fwd_launch_lanes(const void* x, const void* z, const void* U, const void* sw, void* y, void* ws,
+                           size_t ws_bytes, int64_t B, int64_t T, int64_t D, int G, int R, int Rk, int W, int residual,
+                           cudaStream_t st) {
   if (!ws || ws_bytes < lr_tc_fwd_workspace(B, T, Rk, G))
     return set_error(DYNCONV_ERR_WORKSPACE, "lr_fwd (tensor core): workspace too small");
   const int rkp = (Rk + 15) / 16 * 16;

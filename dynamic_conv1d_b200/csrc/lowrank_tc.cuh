@@ -51,6 +51,19 @@ struct ChanGroups {
 
 inline ChanGroups chan_groups(int64_t D, int G) { return ChanGroups{G, (int)((D + kBD - 1) / kBD), (int)D}; }
 
+// Data-parallel peers of the fused backward (dp_comm.cu): every rank's landing
+// buffer [2 parities][world sources][cap floats] and flag counters [world sources]
+// mapped into this process (peer memory over NVLink, plain loads and stores), and
+// this rank's device-side call counter.  world == 1: no cross-GPU reduction.
+constexpr int kMaxWorld = 8;
+struct DpPeers {
+  int world, rank;
+  int64_t cap;                                   // floats per (parity, source) slot
+  float* land[kMaxWorld];                        // rank p's landing buffer
+  unsigned long long* flags[kMaxWorld];          // rank p's per-source float4 counters
+  unsigned long long* epoch;                     // this rank's completed-call count
+};
+
 __host__ __device__ constexpr uint32_t round1024(uint32_t v) { return (v + 1023u) / 1024u * 1024u; }
 
 inline bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; }
@@ -63,9 +76,11 @@ using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t
 EncodeTiledFn encode_fn();
 
 // 3-D bf16 map over a [B][T][D] tensor: dims (D, T, B), box (box_d, box_t, 1).
-// With swizzle128, box_d must be 64 (128-byte rows) and the destination 1024-aligned.
+// swizzle_bytes 0 (none), 32, 64 or 128: box_d * 2 must equal it, and the shared-memory
+// side must be aligned to 8 x swizzle_bytes (16-byte chunk c of row r sits at chunk
+// c ^ ((r >> k) & mask), the pattern TMA and the MMA descriptors share).
 int make_btd_map(CUtensorMap* map, const void* base, int64_t B, int64_t T, int64_t D, int box_d, int box_t,
-                 bool swizzle128 = false);
+                 int swizzle_bytes = 0);
 
 // 4-D bf16 map viewing a [B][T][D] tensor as [B][D/64][T][64] (D % 64 == 0):
 // dims (64, T, D/64, B), box (64, box_t, 2, 1), 128-byte swizzle.  One load then

@@ -21,7 +21,39 @@ from __future__ import annotations
 import torch
 
 from . import _lib
-from .parallel import allreduce_shared_grad, current_group
+from .parallel import allreduce_shared_grad, comm_for, current_group
+
+
+def _fused_dp_backward(lib, group, x, z, U, static_w, dy, dx, dz, dU_f32, ws, B, T, D, R, W, G, code, residual,
+                       stream):
+    """The backward with the sum over data-parallel ranks done inside the kernel
+    (dynconv_lr_bwd_grouped_dp).  Returns (dU [G*R, W*D], dstatic_w [G, W*D] or None),
+    bf16, already summed over the ranks; None when the fused path does not apply
+    (single rank, not bf16, outside the tensor-core envelope), and the caller
+    all-reduces through torch.distributed."""
+    has_static = static_w is not None
+    Rk = R + (1 if has_static else 0)
+    # The choice must be the same on every rank (they all take part in one exchange),
+    # so it rests only on what all ranks share: dtype, W, R_kernel, D, G.
+    if x.dtype != torch.bfloat16 or not (1 <= W <= 4) or Rk > 32 or D % 8 != 0 or (G > 1 and D % 128 != 0):
+        return None
+    if (G * D + 127) // 128 > torch.cuda.get_device_properties(x.device).multi_processor_count:
+        return None
+    comm = comm_for(group, x.device, G * Rk * W * D)
+    if comm is None:
+        return None
+    dU = torch.empty((G * R, W * D), device=x.device, dtype=x.dtype)
+    dsw = torch.empty((G, W * D), device=x.device, dtype=x.dtype) if has_static else None
+    status = lib.dynconv_lr_bwd_grouped_dp(
+        _lib.ptr(x), _lib.ptr(z), _lib.ptr(U), _lib.ptr(static_w), _lib.ptr(dy),
+        _lib.ptr(dx), _lib.ptr(dz), _lib.ptr(dU), _lib.ptr(dsw), _lib.ptr(dU_f32),
+        _lib.ptr(ws), ws.numel(), B, T, D, R, W, G, code, int(residual), comm.ptr, stream,
+    )
+    # Every rank is now committed to the in-kernel exchange: a rank-local refusal (an
+    # unaligned tensor, an empty shard) is an error, not a silent switch to NCCL that
+    # the other ranks would not make.
+    _lib.check(status)
+    return dU, dsw
 
 
 class _LowrankDynamicConvolutionFn(torch.autograd.Function):
@@ -76,18 +108,27 @@ class _LowrankDynamicConvolutionFn(torch.autograd.Function):
         dU_f32 = torch.empty((Rk, W * D), device=x.device, dtype=torch.float32)
         nbytes = lib.dynconv_lr_bwd_workspace_bytes(B, T, D, R, W, code, int(has_static))
         ws = torch.empty(max(int(nbytes), 1), device=x.device, dtype=torch.uint8)
-        reduce_first = ctx.group is not None
-        dU = None if reduce_first else torch.empty_like(U)
-        dsw = None if (reduce_first or not has_static) else torch.empty((W, D), device=x.device, dtype=x.dtype)
         stream = _lib.stream_of(x)
-        _lib.check(
-            lib.dynconv_lr_bwd(
-                _lib.ptr(x), _lib.ptr(z), _lib.ptr(U), _lib.ptr(static_w), _lib.ptr(dy),
-                _lib.ptr(dx), _lib.ptr(dz), _lib.ptr(dU), _lib.ptr(dsw), _lib.ptr(dU_f32),
-                _lib.ptr(ws), ws.numel(),
-                B, T, D, R, W, code, int(ctx.residual), stream,
+        reduce_first = ctx.group is not None
+        fused = None
+        if reduce_first:
+            fused = _fused_dp_backward(lib, ctx.group, x, z, U, static_w, dy, dx, dz, dU_f32, ws,
+                                       B, T, D, R, W, 1, code, ctx.residual, stream)
+        if fused is not None:
+            reduce_first = False  # summed over the ranks and cast inside the kernel
+            dU = fused[0]
+            dsw = fused[1].view(W, D) if has_static else None
+        else:
+            dU = None if reduce_first else torch.empty_like(U)
+            dsw = None if (reduce_first or not has_static) else torch.empty((W, D), device=x.device, dtype=x.dtype)
+            _lib.check(
+                lib.dynconv_lr_bwd(
+                    _lib.ptr(x), _lib.ptr(z), _lib.ptr(U), _lib.ptr(static_w), _lib.ptr(dy),
+                    _lib.ptr(dx), _lib.ptr(dz), _lib.ptr(dU), _lib.ptr(dsw), _lib.ptr(dU_f32),
+                    _lib.ptr(ws), ws.numel(),
+                    B, T, D, R, W, code, int(ctx.residual), stream,
+                )
             )
-        )
         if reduce_first:
             allreduce_shared_grad(dU_f32, ctx.group)
             # one cast of the reduced accumulator; dU and dstatic_w are row views of it
@@ -199,10 +240,17 @@ class _LowrankGroupedFn(torch.autograd.Function):
         dU_f32 = torch.empty((G, Rk, W * D), device=x.device, dtype=torch.float32)
         nbytes = lib.dynconv_lr_bwd_grouped_workspace_bytes(B, T, D, R, W, G, code, int(has_static))
         ws = torch.empty(max(int(nbytes), 1), device=x.device, dtype=torch.uint8)
+        stream = _lib.stream_of(x)
         reduce_first = ctx.group is not None
+        if reduce_first:
+            fused = _fused_dp_backward(lib, ctx.group, x, z, U, static_w, dy, dx, dz, dU_f32, ws,
+                                       B, T, D, R, W, G, code, ctx.residual, stream)
+            if fused is not None:
+                _lib.after_call(dx)
+                dsw = fused[1].view(G, W, D) if has_static else None
+                return dx, dz, fused[0].view(G, R, W * D), dsw, None
         dU = None if reduce_first else torch.empty_like(U)
         dsw = None if (reduce_first or not has_static) else torch.empty_like(static_w)
-        stream = _lib.stream_of(x)
         _lib.check(
             lib.dynconv_lr_bwd_grouped(
                 _lib.ptr(x), _lib.ptr(z), _lib.ptr(U), _lib.ptr(static_w), _lib.ptr(dy),

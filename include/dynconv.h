@@ -195,6 +195,39 @@ int dynconv_lr_bwd_grouped(const void* x, const void* z, const void* U, const vo
                            int64_t B, int64_t T, int64_t D, int64_t R, int64_t W, int64_t G,
                            int dtype, int residual, void* stream);
 
+/* ------------------------------------------- data parallel (fused all-reduce) */
+
+/* A communicator for the fused data-parallel backward: one per rank (one process
+ * per GPU, world 2..8 on one node), made once, before any stream capture.  No
+ * reference counterpart: it replaces the NCCL all-reduce of the float32
+ * shared-gradient buffer that the reference's caller would run after backward.
+ *   1. dynconv_comm_create(world, rank, max_floats, &comm, blob) on each rank, with
+ *      that rank's GPU current: allocates this rank's landing buffer
+ *      (2 x world x max_floats floats) and counters, and writes a blob of
+ *      dynconv_comm_blob_bytes() bytes (CUDA IPC handles, device UUID, rank);
+ *   2. exchange the blobs (any host channel, e.g. torch.distributed), in rank order;
+ *   3. dynconv_comm_connect(comm, blobs) on each rank: maps every peer's buffers
+ *      (refuses two ranks on one GPU);
+ *   4. dynconv_lr_bwd_grouped_dp(...) on every rank, the same number of calls, in the
+ *      same order: dU_f32 (and dU / dstatic_w when given) receive the SUM over all
+ *      ranks, reduced inside the backward kernel over peer memory (NVLink stores,
+ *      bounded waits: a rank that never arrives makes the others' kernels return
+ *      and dynconv_check_device report DYNCONV_ERR_TIMEOUT);
+ *   5. dynconv_comm_destroy(comm) once no rank will call again.
+ * max_floats: a multiple of 4, at least G * R_kernel * W * D of every call. */
+size_t dynconv_comm_blob_bytes(void);
+int dynconv_comm_create(int world, int rank, int64_t max_floats, void** comm, void* blob);
+int dynconv_comm_connect(void* comm, const void* blobs);
+int dynconv_comm_destroy(void* comm);
+/* dynconv_lr_bwd_grouped, with the shared gradients summed over the communicator's
+ * ranks.  Tensor-core path only (bf16, W <= 4, R_kernel <= 32, 16-byte aligned);
+ * otherwise DYNCONV_ERR_UNSUPPORTED. */
+int dynconv_lr_bwd_grouped_dp(const void* x, const void* z, const void* U, const void* static_w, const void* dy,
+                              void* dx, void* dz, void* dU, void* dstatic_w, float* dU_f32,
+                              void* workspace, size_t workspace_bytes,
+                              int64_t B, int64_t T, int64_t D, int64_t R, int64_t W, int64_t G,
+                              int dtype, int residual, void* comm, void* stream);
+
 /* dst[i] = (dtype) src[i], i < n, round-to-nearest-even.  Used after the
  * data-parallel all-reduce of the float32 shared-gradient buffers (replaces
  * dU_fp32.to(U.dtype), lowrank.py:294, and dstatic_accum.to(...), headwise.py:305). */

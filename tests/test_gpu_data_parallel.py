@@ -290,3 +290,116 @@ def test_sequence_parallel_two_gpus(tmp_path):
                        capture_output=True, text=True, timeout=300)
     assert r.returncode == 0, r.stdout[-2000:] + r.stderr[-4000:]
     assert r.stdout.count("ok ") == 4, r.stdout
+
+
+DP2_SCRIPT = textwrap.dedent(
+    """
+    import datetime, os, sys
+    import numpy as np
+    import torch, torch.distributed as dist
+    sys.path.insert(0, {root!r})
+    import oracle
+    from dynamic_conv1d_b200 import data_parallel, lowrank_dynamic_convolution, lowrank_dynamic_convolution_grouped
+    from dynamic_conv1d_b200 import parallel
+    rank, world = int(os.environ["RANK"]), int(os.environ["WORLD_SIZE"])
+    dev = torch.device("cuda", rank)
+    torch.cuda.set_device(dev)
+    dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=60), device_id=dev)
+    g = torch.Generator().manual_seed(21)
+    bf = torch.bfloat16
+    def rnd(*s, scale=1.0):
+        return (torch.randn(*s, generator=g) * scale).to(bf)
+    def rel(a, ref):
+        a = a.detach().float().cpu().numpy().astype(np.float64)
+        return np.linalg.norm(a - ref) / max(np.linalg.norm(ref), 1e-30)
+    f = lambda t: t.float().numpy()
+    B, T, D, R, W = 2 * world, 300, 256, 15, 4
+    x, dy, z = rnd(B, T, D), rnd(B, T, D), rnd(B, T, R, scale=0.5)
+    U, sw = rnd(R, W * D, scale=0.25), rnd(W, D, scale=0.3)
+    rows = slice(2 * rank, 2 * rank + 2)
+    ry = oracle.lowrank_fwd(f(x), f(z), f(U), f(sw), True)
+    rdx, rdz, rdU, rdsw = oracle.lowrank_bwd(f(x), f(z), f(U), f(sw), f(dy), True)
+
+    # eager, three calls (both landing parities, then the first again)
+    for it in range(3):
+        leaves = [x[rows].to(dev).requires_grad_(), z[rows].to(dev).requires_grad_(),
+                  U.to(dev).requires_grad_(), sw.to(dev).requires_grad_()]
+        with data_parallel():
+            y = lowrank_dynamic_convolution(*leaves, residual=True)
+            y.backward(dy[rows].to(dev))
+        torch.cuda.synchronize()
+        assert parallel._comms, "the fused data-parallel path was not used"
+        errs = [rel(y, ry[rows]), rel(leaves[0].grad, rdx[rows]), rel(leaves[1].grad, rdz[rows]),
+                rel(leaves[2].grad, rdU), rel(leaves[3].grad, rdsw)]
+        assert errs[0] <= 1e-2 and max(errs[1:]) <= 2e-2, (it, errs)
+        # every rank holds the same shared gradients, bit for bit
+        for t in (leaves[2].grad, leaves[3].grad):
+            allg = [torch.empty_like(t) for _ in range(world)]
+            dist.all_gather(allg, t.contiguous())
+            assert all(torch.equal(allg[0], a) for a in allg), it
+    print("ok eager", rank, flush=True)
+
+    # grouped (Q/K/V) op: one stacked reduction
+    G = 3
+    xg, dyg, zg = rnd(B, T, G * D), rnd(B, T, G * D), rnd(B, T, G * R, scale=0.5)
+    Ug, swg = rnd(G, R, W * D, scale=0.25), rnd(G, W, D, scale=0.3)
+    leaves = [xg[rows].to(dev).requires_grad_(), zg[rows].to(dev).requires_grad_(),
+              Ug.to(dev).requires_grad_(), swg.to(dev).requires_grad_()]
+    with data_parallel():
+        y = lowrank_dynamic_convolution_grouped(*leaves, residual=True)
+        y.backward(dyg[rows].to(dev))
+    torch.cuda.synchronize()
+    for gi in range(G):
+        sl, slr = slice(gi * D, (gi + 1) * D), slice(gi * R, (gi + 1) * R)
+        _, _, gU, gsw = oracle.lowrank_bwd(f(xg)[..., sl], f(zg)[..., slr], f(Ug[gi]), f(swg[gi]), f(dyg)[..., sl], True)
+        assert rel(leaves[2].grad[gi], gU) <= 2e-2 and rel(leaves[3].grad[gi], gsw) <= 2e-2, gi
+    print("ok grouped", rank, flush=True)
+
+    # the step captured in a CUDA graph and replayed: the call counter lives on the device
+    leaves = [x[rows].to(dev).requires_grad_(), z[rows].to(dev).requires_grad_(),
+              U.to(dev).requires_grad_(), sw.to(dev).requires_grad_()]
+    dyd = dy[rows].to(dev)
+    s = torch.cuda.Stream()
+    s.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(s), data_parallel():
+        for _ in range(2):
+            for l in leaves:
+                l.grad = None
+            lowrank_dynamic_convolution(*leaves, residual=True).backward(dyd)
+    torch.cuda.current_stream().wait_stream(s)
+    torch.cuda.synchronize()
+    for l in leaves:
+        l.grad = None
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph), data_parallel():
+        lowrank_dynamic_convolution(*leaves, residual=True).backward(dyd)
+    for it in range(4):
+        graph.replay()
+        torch.cuda.synchronize()
+        assert rel(leaves[2].grad, rdU) <= 2e-2 and rel(leaves[3].grad, rdsw) <= 2e-2, it
+    from dynamic_conv1d_b200 import _lib
+    _lib.check_device(leaves[0])
+    del graph
+    print("ok graph", rank, flush=True)
+    dist.barrier()
+    dist.destroy_process_group()
+    """
+)
+
+
+def test_fused_data_parallel_two_gpus(tmp_path):
+    """The lowrank backward with the shared-gradient sum done inside the kernel over
+    peer memory (two GPUs): gradients match the full-batch oracle, are bit-identical
+    on both ranks, and stay right over repeated calls and CUDA-graph replays."""
+    import torch
+
+    if not torch.cuda.is_available() or torch.cuda.device_count() < 2:
+        pytest.skip("needs two CUDA devices")
+    script = tmp_path / "dp2.py"
+    script.write_text(DP2_SCRIPT.format(root=ROOT))
+    r = subprocess.run([sys.executable, "-m", "torch.distributed.run", "--nnodes=1", "--nproc-per-node", "2",
+                        "--master-addr", "127.0.0.1", "--master-port", str(_free_port()), str(script)],
+                       capture_output=True, text=True, timeout=300)
+    assert r.returncode == 0, r.stdout[-2000:] + r.stderr[-4000:]
+    for tag in ("ok eager", "ok grouped", "ok graph"):
+        assert r.stdout.count(tag) == 2, r.stdout
