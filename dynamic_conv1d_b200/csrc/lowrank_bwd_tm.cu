@@ -33,8 +33,8 @@
 // 40 MMAs per 8192 (step, channel) pairs at R_kernel <= 16.
 //
 // Warps: 0 producer (TMA: z per tile, dy and x per 64-channel half tile into a
-// ring), 1 weight MMAs + TMEM owner, 2/3 dz and dU MMAs of chunk parity 0/1
-// (separate dz accumulators, summed at readout), 4..19 the epilogue in two teams of eight (team = chunk parity; a warp has 32 steps of its
+// ring), 1 weight MMAs + TMEM owner, 2/3 dz MMAs and 4/5 dU MMAs of chunk parity
+// 0/1 (separate dz accumulators, summed at readout), 6..21 the epilogue in two teams of eight (team = chunk parity; a warp has 32 steps of its
 // TMEM lane quarter and 16 channels of the chunk).  The dz partial of this CTA's
 // 128 channels goes to the workspace and is summed across channel blocks after a
 // grid-wide count (cooperative launch), as is dU across token groups.  Every wait
@@ -54,7 +54,7 @@ constexpr int kTT = 128;               // steps per tile
 constexpr int kCh = 32;                // channels per chunk
 constexpr int kRowsXY = kTT + 3;       // rows of a dy / x box (W - 1 <= 3 halo rows)
 constexpr int kZR = 136;               // z rows per tile (128 + W - 1, padded)
-constexpr int kCtl = 4;                // producer + three MMA issuers
+constexpr int kCtl = 6;                // producer + five MMA issuers
 constexpr int kEpi = 16;               // epilogue warps
 constexpr int kThreads = 32 * (kCtl + kEpi);
 
@@ -189,10 +189,10 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     for (int b2 = 0; b2 < 2; ++b2) {
       mbar_init(&zfull[b2], 1);
-      mbar_init(&zempty[b2], 3);    // the weight MMAs and both dz/dU issuers of the tile
+      mbar_init(&zempty[b2], 3);    // the weight MMAs and both dU issuers of the tile
       mbar_init(&pfull[b2], kEpi / 2);
-      mbar_init(&pempty[b2], 1);    // the dz and dU MMAs of the chunk (one issuer)
-      mbar_init(&dzfull[b2], 2);    // both dz/dU issuers
+      mbar_init(&pempty[b2], 2);    // the dz and the dU MMAs of the chunk
+      mbar_init(&dzfull[b2], 2);    // both dz issuers
       mbar_init(&dzempty[b2], kEpi);
     }
     for (int c = 0; c < NWB; ++c) {
@@ -289,11 +289,13 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       if (!ok) break;
     }
-  } else if (warp == 2 || warp == 3) {
-    // ------------------------------------------------------------ dz and dU MMAs (chunk parity tau)
-    const int tau = warp - 2;
-    const uint32_t idesc_z = make_idesc_bf16(kTT, RKP, 0, 0);  // dz: A = P (K-major), B = U (K-major)
-    const uint32_t idesc_u = make_idesc_bf16(kTT, RKP, 1, 1);  // dU: A = P (MN-major), B = z (MN-major)
+  } else if (warp >= 2 && warp <= 5) {
+    // ------------------------------------------------------------ dz (warps 2/3) and dU (4/5) MMAs of
+    // chunk parity tau: separate issuers, so a chunk's 16 MMAs go out in two parallel streams
+    const bool is_dz = warp < 4;
+    const int tau = (warp - 2) & 1;
+    const uint32_t idesc = is_dz ? make_idesc_bf16(kTT, RKP, 0, 0)   // dz: A = P (K-major), B = U (K-major)
+                                 : make_idesc_bf16(kTT, RKP, 1, 1);  // dU: A = P (MN-major), B = z (MN-major)
     const uint32_t pb = smem_u32(smem + L::kOffP + tau * L::kPBuf);
     const uint32_t ub = smem_u32(smem + L::kOffU);
     const uint32_t zb0 = smem_u32(smem + L::kOffZ);
@@ -302,42 +304,44 @@ __global__ void __launch_bounds__(kThreads, 1)
       bool ok = true;
       for (int j = tau; j < 4; j += 2, ++m) {
         if (!mbar_wait(&pfull[tau], m & 1, kErrWaitMma, &abort_flag) ||
-            (j == tau && !mbar_wait(&dzempty[k & 1], ((k >> 1) & 1) ^ 1, kErrWaitMma, &abort_flag)) ||
-            (j == tau && !mbar_wait(&zfull[k & 1], (k >> 1) & 1, kErrWaitMma, &abort_flag))) {
+            (j == tau && is_dz && !mbar_wait(&dzempty[k & 1], ((k >> 1) & 1) ^ 1, kErrWaitMma, &abort_flag)) ||
+            (j == tau && !is_dz && !mbar_wait(&zfull[k & 1], (k >> 1) & 1, kErrWaitMma, &abort_flag))) {
           ok = false;
           break;
         }
         tc_fence_after();
         if (lane == 0) {
-          const uint32_t dacc = tmem + L::kColDZ + (tau * 2 + (k & 1)) * RKP;
+          if (is_dz) {
+            const uint32_t dacc = tmem + L::kColDZ + (tau * 2 + (k & 1)) * RKP;
 #pragma unroll
-          for (int w = 0; w < W; ++w) {
+            for (int w = 0; w < W; ++w) {
 #pragma unroll
-            for (int h2 = 0; h2 < 2; ++h2) {
-              const uint64_t ad = make_smem_desc(pb + (w * 4 + 2 * h2) * 128, 128, 2048);
-              const uint64_t bd = make_smem_desc(ub + w * L::kUTap + (4 * j + 2 * h2) * L::kUcg, L::kUcg, 128);
-              umma_f16(dacc, ad, bd, idesc_z, (j == tau && w == 0 && h2 == 0) ? 0u : 1u);
+              for (int h2 = 0; h2 < 2; ++h2) {
+                const uint64_t ad = make_smem_desc(pb + (w * 4 + 2 * h2) * 128, 128, 2048);
+                const uint64_t bd = make_smem_desc(ub + w * L::kUTap + (4 * j + 2 * h2) * L::kUcg, L::kUcg, 128);
+                umma_f16(dacc, ad, bd, idesc, (j == tau && w == 0 && h2 == 0) ? 0u : 1u);
+              }
             }
-          }
-          const uint32_t uacc = tmem + L::kColDU + j * RKP;
-          const uint32_t zb = zb0 + (k & 1) * L::kZBytes;
+            umma_commit(&pempty[tau]);
+            if (j == tau + 2) umma_commit(&dzfull[k & 1]);
+          } else {
+            const uint32_t uacc = tmem + L::kColDU + j * RKP;
+            const uint32_t zb = zb0 + (k & 1) * L::kZBytes;
 #pragma unroll
-          for (int s8 = 0; s8 < kTT / 16; ++s8) {
-            const uint64_t ad = make_smem_desc(pb + s8 * 4096, 2048, 128);
-            const uint64_t bd = make_smem_desc(zb + s8 * 256, 128, L::kLZ);
-            umma_f16(uacc, ad, bd, idesc_u, (k == 0 && s8 == 0) ? 0u : 1u);
-          }
-          umma_commit(&pempty[tau]);
-          if (j == tau + 2) {
-            umma_commit(&dzfull[k & 1]);
-            umma_commit(&zempty[k & 1]);
+            for (int s8 = 0; s8 < kTT / 16; ++s8) {
+              const uint64_t ad = make_smem_desc(pb + s8 * 4096, 2048, 128);
+              const uint64_t bd = make_smem_desc(zb + s8 * 256, 128, L::kLZ);
+              umma_f16(uacc, ad, bd, idesc, (k == 0 && s8 == 0) ? 0u : 1u);
+            }
+            umma_commit(&pempty[tau]);
+            if (j == tau + 2) umma_commit(&zempty[k & 1]);
           }
         }
         __syncwarp();
       }
       if (!ok) break;
     }
-    if (lane == 0) umma_commit(&du_bar);
+    if (!is_dz && lane == 0) umma_commit(&du_bar);
     __syncwarp();
   } else {
     // ------------------------------------------------------------ epilogue
@@ -385,19 +389,20 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int c = 4 * k + j, wb = c % NWB, hs = 2 * k + (j >> 1), s = hs % S;
         if (!dead) dead = !mbar_wait(&wfull[wb], (c / NWB) & 1, kErrWaitEpilogue, &abort_flag);
         if (!dead) dead = !mbar_wait(&rfull[s], (hs / S) & 1, kErrWaitEpilogue, &abort_flag);
-        if (!dead) dead = !mbar_wait(&pempty[tau], (m & 1) ^ 1, kErrWaitEpilogue, &abort_flag);
         tc_fence_after();
         // this warp's dx sub-tile buffer (m & 1) is free once its store of chunk m-2 has read it
         uint8_t* const stg = smem + L::kOffStage + (e * 2 + (m & 1)) * L::kStage;
         if (lane == 0 && !dead) bulk_wait_group_read<1>();
         __syncwarp();
+        const uint8_t* dys = smem + L::kOffRing + s * L::kSlot;
+        const uint8_t* xs = dys + L::kBoxStride;
+        // ---- dx (needs the weights and dy): first, while the MMAs of this team's previous
+        // chunk may still be reading its P buffer
         if (!dead) {
-          const uint8_t* dys = smem + L::kOffRing + s * L::kSlot;
-          const uint8_t* xs = dys + L::kBoxStride;
           const uint32_t wcol = ta + L::kColW + wb * 128 + 16 * h;  // this warp's 16 channels, tap 0
           // The weights arrive in four batches (8-channel group cgi, 4-channel half hh) of
           // W x 4 values.  Each batch's tensor-memory load is issued one step ahead, so
-          // its latency overlaps the P products or the previous batch's dx.
+          // its latency overlaps the dy loads or the previous batch's dx.
           float wa[W][4], wb2[W][4];
           auto ld_w = [&](float (&v)[W][4], int cgi, int hh) {
 #pragma unroll
@@ -424,45 +429,64 @@ __global__ void __launch_bounds__(kThreads, 1)
             p1 = pack_bf16x2(a1.x, a1.y);
           };
           ld_w(wa, 0, 0);
+          // both 8-channel groups' dy rows t .. t+W-1, loaded before any store
+          uint4 dyr[2][W];
 #pragma unroll
           for (int cgi = 0; cgi < 2; ++cgi) {
-            const int cgc = 2 * h + cgi;        // 8-channel group within the chunk
-            const int cc = (j & 1) * 4 + cgc;   // 16-byte chunk within the half tile's 128-byte row
-            uint4 dyr[W];
+            const int cc = (j & 1) * 4 + 2 * h + cgi;  // 16-byte chunk within the half tile's 128-byte row
 #pragma unroll
             for (int w = 0; w < W; ++w) {
               const int r = t + w;
-              dyr[w] = *reinterpret_cast<const uint4*>(dys + r * 128 + ((cc ^ (r & 7)) << 4));
+              dyr[cgi][w] = *reinterpret_cast<const uint4*>(dys + r * 128 + ((cc ^ (r & 7)) << 4));
             }
-            // P_w[t] = bf16(dy[t] * x[t-w]) -> block (t/8, w, cgc) of the team's P buffer
-            {
-              const uint32_t* d0w = reinterpret_cast<const uint32_t*>(&dyr[0]);
+          }
+          uint32_t pk[2][4];
 #pragma unroll
-              for (int w = 0; w < W; ++w) {
-                const int r = t - w + 3;
-                const uint4 xr = *reinterpret_cast<const uint4*>(xs + r * 128 + ((cc ^ (r & 7)) << 4));
-                *reinterpret_cast<uint4*>(pbuf + (w * 4 + cgc) * 128) =
-                    make_uint4(mul_bf16x2(d0w[0], xr.x), mul_bf16x2(d0w[1], xr.y), mul_bf16x2(d0w[2], xr.z),
-                               mul_bf16x2(d0w[3], xr.w));
-              }
-            }
-            uint32_t pk[4];
+          for (int cgi = 0; cgi < 2; ++cgi) {
             tmem_ld_wait();          // batch (cgi, 0) in wa
             ld_w(wb2, cgi, 1);
-            dx4(wa, dyr, 0, pk[0], pk[1]);
+            dx4(wa, dyr[cgi], 0, pk[cgi][0], pk[cgi][1]);
             tmem_ld_wait();          // batch (cgi, 1) in wb2
             if (cgi == 0) ld_w(wa, 1, 0);
-            dx4(wb2, dyr, 1, pk[2], pk[3]);
-            // row `lane` of the [32 steps][16 ch] sub-tile, 32-byte swizzle (conflict-free)
+            dx4(wb2, dyr[cgi], 1, pk[cgi][2], pk[cgi][3]);
+          }
+#pragma unroll
+          for (int cgi = 0; cgi < 2; ++cgi)  // rows of the [32 steps][16 ch] sub-tile, 32-byte swizzle
             *reinterpret_cast<uint4*>(stg + lane * 32 + ((cgi ^ ((lane >> 2) & 1)) << 4)) =
-                make_uint4(pk[0], pk[1], pk[2], pk[3]);
+                make_uint4(pk[cgi][0], pk[cgi][1], pk[cgi][2], pk[cgi][3]);
+        }
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&wempty[wb]);  // the weights are in registers: the buffer is free
+        // ---- P_w[t] = bf16(dy[t] * x[t-w]) -> block (t/8, w, cgc) of the team's P buffer, once
+        // the MMAs of the team's previous chunk are done with it
+        if (!dead) dead = !mbar_wait(&pempty[tau], (m & 1) ^ 1, kErrWaitEpilogue, &abort_flag);
+        if (!dead) {
+          // every load of the section first (the compiler cannot move a load above a store
+          // into the same shared memory), then the products and the stores
+          uint4 d0v[2], xr[2][W];
+#pragma unroll
+          for (int cgi = 0; cgi < 2; ++cgi) {
+            const int cc = (j & 1) * 4 + 2 * h + cgi;
+            d0v[cgi] = *reinterpret_cast<const uint4*>(dys + t * 128 + ((cc ^ (t & 7)) << 4));
+#pragma unroll
+            for (int w = 0; w < W; ++w) {
+              const int r = t - w + 3;
+              xr[cgi][w] = *reinterpret_cast<const uint4*>(xs + r * 128 + ((cc ^ (r & 7)) << 4));
+            }
+          }
+#pragma unroll
+          for (int cgi = 0; cgi < 2; ++cgi) {
+#pragma unroll
+            for (int w = 0; w < W; ++w)
+              *reinterpret_cast<uint4*>(pbuf + (w * 4 + 2 * h + cgi) * 128) =
+                  make_uint4(mul_bf16x2(d0v[cgi].x, xr[cgi][w].x), mul_bf16x2(d0v[cgi].y, xr[cgi][w].y),
+                             mul_bf16x2(d0v[cgi].z, xr[cgi][w].z), mul_bf16x2(d0v[cgi].w, xr[cgi][w].w));
           }
         }
         fence_proxy_async_smem();  // P and the dx sub-tile, for the MMAs and the TMA store
-        tc_fence_before();
         __syncwarp();
         if (lane == 0) {
-          mbar_arrive(&wempty[wb]);
           mbar_arrive(&pfull[tau]);
           mbar_arrive(&rempty[s]);
           if (!dead) {

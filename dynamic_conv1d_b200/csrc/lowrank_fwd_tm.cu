@@ -72,6 +72,34 @@ struct FtSplit {
   int64_t n_units;  // n_dblk * n_tiles, split evenly over the grid
 };
 
+// Walks a CTA's units in order without divisions: (channel block, tile) and the
+// tile's batch row b and first step t0.
+struct UnitCursor {
+  int dblk, tile, b, t0;
+  __device__ __forceinline__ void init(int64_t u, const FtSplit& sp) {
+    dblk = (int)(u / sp.n_tiles);
+    tile = (int)(u - (int64_t)dblk * sp.n_tiles);
+    b = tile / sp.tiles_row;
+    t0 = (tile - b * sp.tiles_row) * kTT;
+  }
+  // advance one unit; true when the channel block changed
+  __device__ __forceinline__ bool next(const FtSplit& sp) {
+    ++tile;
+    t0 += kTT;
+    if (t0 >= sp.tiles_row * kTT) {
+      t0 = 0;
+      ++b;
+    }
+    if (tile == sp.n_tiles) {
+      tile = 0;
+      b = 0;
+      ++dblk;
+      return true;
+    }
+    return false;
+  }
+};
+
 // U_ext block of channels [dlb, dlb + 128) of one group as 8 x 8 blocks
 // [tap][ch/8][r/8][8 r][8 ch] -- the MN-major B operand (N = channels, K = ranks).
 template <int W, int RKP, int NT>
@@ -147,20 +175,17 @@ __global__ void __launch_bounds__(kThreads, 1)
   tc_fence_after();
   const uint32_t tmem = tmem_slot;
 
-  // channel block of local unit kk; a CTA's units form segments of one channel block
-  auto dblk_of = [&](int kk) { return (int)((u0 + kk) / sp.n_tiles); };
-
   if (warp == 0) {
     // ------------------------------------------------------------ producer
     if (lane == 0) {
       const uint64_t pol = policy_evict_first();
       const uint64_t pol_z = policy_evict_normal();  // z rows are read by every channel block
       int hs = 0;
-      for (int k = 0; k < n; ++k) {
-        const int64_t u = u0 + k;
-        const int dblk = (int)(u / sp.n_tiles), tile = (int)(u % sp.n_tiles);
-        const int b = tile / sp.tiles_row, t0 = (tile % sp.tiles_row) * kTT;
-        const int d0 = dblk * kBD, grp = dblk / cg.nd;
+      UnitCursor uc;
+      uc.init(u0, sp);
+      for (int k = 0; k < n; ++k, uc.next(sp)) {
+        const int b = uc.b, t0 = uc.t0;
+        const int d0 = uc.dblk * kBD, grp = uc.dblk / cg.nd;
         if (!mbar_wait(&zempty[k & 1], ((k >> 1) & 1) ^ 1, kErrWaitProducer, &abort_flag)) break;
         mbar_arrive_expect_tx(&zfull[k & 1], L::kZBytes);
         tma_load_4d(smem + L::kOffZ + (k & 1) * L::kZBytes, &zmap, &zfull[k & 1], 0, t0, b, grp * (RKP / 8), pol_z);
@@ -186,8 +211,10 @@ __global__ void __launch_bounds__(kThreads, 1)
       const uint32_t ub = smem_u32(smem + L::kOffU);
       const uint32_t zb0 = smem_u32(smem + L::kOffZ);
       int useg = 0;  // U segments started
+      UnitCursor uc;
+      uc.init(u0, sp);
       for (int k = 0; k < n; ++k) {
-        if (k > 0 && dblk_of(k) != dblk_of(k - 1)) {
+        if (k > 0 && uc.next(sp)) {
           // new channel block: the U buffer is free once this issuer's MMAs so far are done
           if (lane == 0) umma_commit(&ufree);
           __syncwarp();
@@ -233,10 +260,12 @@ __global__ void __launch_bounds__(kThreads, 1)
       bool dead = false;
       int useg = 0;
       int m = 0;  // chunks this warp has handled
+      UnitCursor uc;
+      uc.init(u0, sp);
       for (int k = 0; k < n; ++k) {
-        const int64_t u = u0 + k;
-        const int dblk = (int)(u / sp.n_tiles), tile = (int)(u % sp.n_tiles);
-        if (k == 0 || dblk != dblk_of(k - 1)) {
+        const bool new_block = k == 0 || uc.next(sp);
+        const int dblk = uc.dblk;
+        if (new_block) {
           // U block of a new channel block (the first one, or a reload once both
           // issuers have finished every MMA that reads the old block)
           if (k > 0) {
@@ -252,7 +281,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           __syncwarp();
           if (lane == 0) mbar_arrive(&uready);
         }
-        const int b = tile / sp.tiles_row, t0 = (tile % sp.tiles_row) * kTT;
+        const int b = uc.b, t0 = uc.t0;
         const int d0 = dblk * kBD;
         for (int j = tau; j < 4; j += 2, ++m) {
           const int c = 4 * k + j, wb = c % kNWB, hs = 2 * k + (j >> 1), s = hs % S;
@@ -294,27 +323,31 @@ __global__ void __launch_bounds__(kThreads, 1)
               p1 = pack_bf16x2(a1.x, a1.y);
             };
             ld_w(wa, 0, 0);
+            // both 8-channel groups' x rows t-W+1 .. t, loaded before any store
+            uint4 xr[2][W];
 #pragma unroll
             for (int cgi = 0; cgi < 2; ++cgi) {
-              const int cgc = 2 * h + cgi;       // 8-channel group within the chunk
-              const int cc = (j & 1) * 4 + cgc;  // 16-byte chunk within the half tile's 128-byte row
-              uint4 xr[W];
+              const int cc = (j & 1) * 4 + 2 * h + cgi;  // 16-byte chunk within the half tile's 128-byte row
 #pragma unroll
               for (int w = 0; w < W; ++w) {
                 const int r = t - w + 3;
-                xr[w] = *reinterpret_cast<const uint4*>(xs + r * 128 + ((cc ^ (r & 7)) << 4));
+                xr[cgi][w] = *reinterpret_cast<const uint4*>(xs + r * 128 + ((cc ^ (r & 7)) << 4));
               }
-              uint32_t pk[4];
+            }
+            uint32_t pk[2][4];
+#pragma unroll
+            for (int cgi = 0; cgi < 2; ++cgi) {
               tmem_ld_wait();  // batch (cgi, 0) in wa
               ld_w(wb2, cgi, 1);
-              y4(wa, xr, 0, pk[0], pk[1]);
+              y4(wa, xr[cgi], 0, pk[cgi][0], pk[cgi][1]);
               tmem_ld_wait();  // batch (cgi, 1) in wb2
               if (cgi == 0) ld_w(wa, 1, 0);
-              y4(wb2, xr, 1, pk[2], pk[3]);
-              // row `lane` of the [32 steps][16 ch] sub-tile, 32-byte swizzle (conflict-free)
-              *reinterpret_cast<uint4*>(stg + lane * 32 + ((cgi ^ ((lane >> 2) & 1)) << 4)) =
-                  make_uint4(pk[0], pk[1], pk[2], pk[3]);
+              y4(wb2, xr[cgi], 1, pk[cgi][2], pk[cgi][3]);
             }
+#pragma unroll
+            for (int cgi = 0; cgi < 2; ++cgi)  // rows of the [32 steps][16 ch] sub-tile, 32-byte swizzle
+              *reinterpret_cast<uint4*>(stg + lane * 32 + ((cgi ^ ((lane >> 2) & 1)) << 4)) =
+                  make_uint4(pk[cgi][0], pk[cgi][1], pk[cgi][2], pk[cgi][3]);
           }
           fence_proxy_async_smem();  // the y sub-tile, for the TMA store
           tc_fence_before();
