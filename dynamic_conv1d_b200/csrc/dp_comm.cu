@@ -12,8 +12,9 @@
 // all-reduce replaces the NCCL collective that followed the kernel.  Only plain
 // stores, loads and atomics touch peer memory (no TMA, no switch-side reduction).
 //
-// The counters are cumulative and the call count lives on the device (advanced
-// by the kernel), so the kernels can be captured in a CUDA graph and replayed.
+// The counters are cumulative, and the call count and the delivered total live on
+// the device (advanced by the kernel), so calls may differ in size and the kernels
+// can be captured in a CUDA graph and replayed.
 // Landing slots alternate by call parity: a rank can only be two calls ahead of a
 // peer once that peer has finished reading the older call's slot (a call's
 // kernel waits for every peer's contribution to that call).
@@ -31,7 +32,7 @@ struct Comm {
   int64_t cap = 0;             // floats per (parity, source) slot
   float* land = nullptr;       // own landing buffer
   unsigned long long* flags = nullptr;  // own counters [world]
-  unsigned long long* epoch = nullptr;  // own call counter
+  unsigned long long* epoch = nullptr;  // own [calls completed, float4s delivered per source]
   bool connected = false;
   float* peer_land[lrtc::kMaxWorld] = {};
   unsigned long long* peer_flags[lrtc::kMaxWorld] = {};
@@ -90,8 +91,8 @@ int dynconv_comm_create(int world, int rank, int64_t max_floats, void** comm, vo
   c->cap = max_floats;
   cudaError_t e = cudaGetDevice(&c->device);
   if (e == cudaSuccess) e = cudaMalloc(&c->land, (size_t)2 * world * max_floats * sizeof(float));
-  if (e == cudaSuccess) e = cudaMalloc(&c->flags, (size_t)(world + 1) * sizeof(unsigned long long));
-  if (e == cudaSuccess) e = cudaMemset(c->flags, 0, (size_t)(world + 1) * sizeof(unsigned long long));
+  if (e == cudaSuccess) e = cudaMalloc(&c->flags, (size_t)(world + 2) * sizeof(unsigned long long));
+  if (e == cudaSuccess) e = cudaMemset(c->flags, 0, (size_t)(world + 2) * sizeof(unsigned long long));
   if (e == cudaSuccess) c->epoch = c->flags + world;
   Blob b;
   memset(&b, 0, sizeof(b));

@@ -170,7 +170,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   __shared__ uint32_t tmem_slot;
   __shared__ int abort_flag;
   __shared__ int grp_ok;
-  __shared__ unsigned long long dp_epoch_s;
+  __shared__ unsigned long long dp_epoch_s, dp_base_s;
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int dblk = blockIdx.x % sp.n_dblk;
@@ -201,8 +201,10 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     mbar_init(&du_bar, 2);
     abort_flag = 0;
-    // calls completed so far (data-parallel counter; read before any CTA of this launch advances it)
-    dp_epoch_s = peers.world > 1 ? *reinterpret_cast<volatile unsigned long long*>(peers.epoch) : 0ull;
+    // data-parallel call counter and the float4s each source has delivered so far (calls
+    // may differ in size); read before any CTA of this launch advances them
+    dp_epoch_s = peers.world > 1 ? reinterpret_cast<volatile unsigned long long*>(peers.epoch)[0] : 0ull;
+    dp_base_s = peers.world > 1 ? reinterpret_cast<volatile unsigned long long*>(peers.epoch)[1] : 0ull;
     fence_barrier_init();
   }
   if (warp == 0 && lane == 0) {
@@ -212,7 +214,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     prefetch_tensormap(&dxmap);
   }
   __syncthreads();  // barriers initialised: the producer starts its loads at once
-  const unsigned long long dp_epoch = dp_epoch_s;
+  const unsigned long long dp_epoch = dp_epoch_s, dp_base = dp_base_s;
   uint32_t tmem = 0;
   if (warp != 0) {
     constexpr int kNonProducer = kThreads - 32;
@@ -656,7 +658,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     // Publish: every thread's peer stores, then one system-scope fence per thread,
     // the CTA barrier, and this CTA's count of float4s added to every rank's counter
     // for this source.  Then wait until every source has delivered all n4 float4s of
-    // this call (counters are cumulative: call c completes at (c + 1) * n4) and sum
+    // this call (counters are cumulative: this call completes at the delivered total
+    // before it plus n4) and sum
     // the world sources in rank order -- the same order on every rank, so all ranks
     // hold bit-identical results.
     __threadfence_system();
@@ -666,7 +669,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (ok)
         for (int p2 = 0; p2 < peers.world; ++p2)
           atomicAdd_system(peers.flags[p2] + peers.rank, (unsigned long long)(hi - lo));
-      const unsigned long long target = (dp_epoch + 1) * (unsigned long long)n4;
+      const unsigned long long target = dp_base + (unsigned long long)n4;
       const uint64_t tstart = globaltimer_ns();
       for (int src = 0; ok && src < peers.world; ++src) {
         const volatile unsigned long long* f = peers.flags[peers.rank] + src;
@@ -695,8 +698,11 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         finish(i, a4);
       }
-      // one CTA advances the call counter; every CTA of this launch read it at the start
-      if (blockIdx.x == 0 && threadIdx.x == 0) *peers.epoch = dp_epoch + 1;
+      // one CTA advances the counters; every CTA of this launch read them at the start
+      if (blockIdx.x == 0 && threadIdx.x == 0) {
+        peers.epoch[0] = dp_epoch + 1;
+        peers.epoch[1] = dp_base + (unsigned long long)n4;
+      }
     }
   }
   tc_fence_before();

@@ -61,7 +61,7 @@ struct DpPeers {
   int64_t cap;                                   // floats per (parity, source) slot
   float* land[kMaxWorld];                        // rank p's landing buffer
   unsigned long long* flags[kMaxWorld];          // rank p's per-source float4 counters
-  unsigned long long* epoch;                     // this rank's completed-call count
+  unsigned long long* epoch;                     // this rank's [calls completed, float4s per source so far]
 };
 
 __host__ __device__ constexpr uint32_t round1024(uint32_t v) { return (v + 1023u) / 1024u * 1024u; }
