@@ -84,9 +84,7 @@ int sm_count() {
 }
 
 unsigned int lr_tc_error_word();
-unsigned int lr_bwd_error_word();
 unsigned int lr_bwd_tm_error_word();
-unsigned int lr_fwd_tm_error_word();
 unsigned int hw_tma_error_word();
 bool hw_tma_supported(int64_t D, int64_t H, int W, int log2hs, int dtype, const void* const* ptrs, int nptrs);
 int hw_tma_partial_rows(int64_t B, int64_t T, int64_t D, int log2hs);
@@ -187,13 +185,12 @@ int dynconv_check_device(void* stream) {
   cudaError_t e = cudaStreamSynchronize(st);
   if (e != cudaSuccess) return cuda_status(e, "cudaStreamSynchronize");
   // every word is read (and so cleared) before the first non-zero one is reported
-  const unsigned int words[6] = {lr_tc_error_word(), lr_fwd_tm_error_word(), lr_bwd_error_word(),
-                                 lr_bwd_tm_error_word(), selftest_error_word(), hw_tma_error_word()};
-  static const char* const kFile[6] = {"lowrank forward", "lowrank forward", "lowrank backward", "lowrank backward",
-                                       "self-test", "headwise"};
+  const unsigned int words[4] = {lr_tc_error_word(), lr_bwd_tm_error_word(), selftest_error_word(),
+                                 hw_tma_error_word()};
+  static const char* const kFile[4] = {"lowrank forward", "lowrank backward", "self-test", "headwise"};
   for (unsigned int v : words)
     if (v == 0xFFFFFFFFu) return set_error(DYNCONV_ERR_CUDA, "could not read the device error word");
-  for (int i = 0; i < 6; ++i)
+  for (int i = 0; i < 4; ++i)
     if (words[i] != 0)
       return set_error(DYNCONV_ERR_TIMEOUT, "a device-side bounded wait gave up (%s kernel, site %u)", kFile[i],
                        words[i]);

@@ -807,8 +807,25 @@ int launch_tm_w(int W, const void* x, const void* z, const void* U, const void* 
 
 }  // namespace
 
+// Tensor-core backward envelope: bf16, W <= 4, R_kernel <= 32, D % 8 == 0 (TMA row
+// pitch; D % 128 == 0 with G > 1 channel groups), 16-byte aligned activations (TMA
+// base), grid co-resident.  Everything else runs the CUDA-core kernels of
+// lowrank_simple.cu (G = 1 only).
+bool lr_tc_bwd_supported(int64_t D, int Rk, int W, int dtype, const void* const* ptrs, int nptrs, int G) {
+  if (dtype != DYNCONV_DTYPE_BF16 || W < 1 || W > 4 || Rk < 1 || Rk > 32 || D % 8 != 0) return false;
+  if (G < 1 || (G > 1 && D % kBD != 0)) return false;
+  if (((int64_t)G * D + kBD - 1) / kBD > sm_count()) return false;  // the cooperative grid must fit on the GPU
+  for (int i = 0; i < nptrs; ++i)
+    if (ptrs[i] && !aligned16(ptrs[i])) return false;
+  return encode_fn() != nullptr || nptrs == 0;
+}
+
 size_t lr_tm_bwd_workspace(int64_t B, int64_t T, int64_t D, int Rk, int W, int G) {
   return tm_workspace(nullptr, B, T, D, Rk, W, G).bytes;
+}
+
+size_t lr_tc_bwd_workspace(int64_t B, int64_t T, int64_t D, int Rk, int W, int G) {
+  return lr_tm_bwd_workspace(B, T, D, Rk, W, G);
 }
 
 // peers == nullptr: single-GPU result.  Otherwise dU_f32 / dU / dstatic_w receive the
@@ -829,6 +846,13 @@ int lr_tm_bwd_launch(const void* x, const void* z, const void* U, const void* sw
   if (Rk <= 16)
     return launch_tm_w<16>(W, x, z, U, sw, dy, dx, dz, dU_f32, dU, dsw, ws, B, T, D, G, R, Rk, residual, pr, st);
   return launch_tm_w<32>(W, x, z, U, sw, dy, dx, dz, dU_f32, dU, dsw, ws, B, T, D, G, R, Rk, residual, pr, st);
+}
+
+int lr_tc_bwd_launch(const void* x, const void* z, const void* U, const void* sw, const void* dy, void* dx, void* dz,
+                     float* dU_f32, void* dU, void* dsw, void* ws, size_t ws_bytes, int64_t B, int64_t T, int64_t D,
+                     int G, int R, int Rk, int W, int residual, cudaStream_t st) {
+  return lr_tm_bwd_launch(x, z, U, sw, dy, dx, dz, dU_f32, dU, dsw, ws, ws_bytes, B, T, D, G, R, Rk, W, residual,
+                          nullptr, st);
 }
 
 }  // namespace dynconv

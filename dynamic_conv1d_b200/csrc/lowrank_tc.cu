@@ -72,22 +72,6 @@ int make_btd_map(CUtensorMap* map, const void* base, int64_t B, int64_t T, int64
   return DYNCONV_OK;
 }
 
-int make_btd4_map(CUtensorMap* map, const void* base, int64_t B, int64_t T, int64_t D, int box_t) {
-  EncodeTiledFn fn = encode_fn();
-  if (!fn) return set_error(DYNCONV_ERR_CUDA, "cuTensorMapEncodeTiled unavailable");
-  if (D % 64 != 0) return set_error(DYNCONV_ERR_SHAPE, "4-D channel-group map needs D %% 64 == 0");
-  if (int s = ensure_context()) return s;
-  cuuint64_t dims[4] = {64, (cuuint64_t)T, (cuuint64_t)(D / 64), (cuuint64_t)B};
-  cuuint64_t strides[3] = {(cuuint64_t)D * 2, 128, (cuuint64_t)T * D * 2};
-  cuuint32_t box[4] = {64, (cuuint32_t)box_t, 2, 1};
-  cuuint32_t estr[4] = {1, 1, 1, 1};
-  CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 4, const_cast<void*>(base), dims, strides, box, estr,
-                  CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
-                  CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
-  if (r != CUDA_SUCCESS) return set_error(DYNCONV_ERR_CUDA, "cuTensorMapEncodeTiled(4-D) failed (%d)", (int)r);
-  return DYNCONV_OK;
-}
-
 int make_zpack_map(CUtensorMap* map, const void* base, int64_t B, int64_t T, int rkp, int rows, int G) {
   EncodeTiledFn fn = encode_fn();
   if (!fn) return set_error(DYNCONV_ERR_CUDA, "cuTensorMapEncodeTiled unavailable");
@@ -399,19 +383,8 @@ size_t lr_tc_fwd_workspace(int64_t B, int64_t T, int Rk, int G) {
   return zpack_bytes(B, T, (Rk + 15) / 16 * 16, G);
 }
 
-int lr_tm_fwd_launch(const void* x, const void* z, const void* U, const void* sw, void* y, void* ws, int64_t B,
-                     int64_t T, int64_t D, int G, int R, int Rk, int W, int residual, cudaStream_t st);
-
 int lr_tc_fwd_launch(const void* x, const void* z, const void* U, const void* sw, void* y, void* ws, size_t ws_bytes,
                      int64_t B, int64_t T, int64_t D, int G, int R, int Rk, int W, int residual, cudaStream_t st) {
-  if (!ws || ws_bytes < lr_tc_fwd_workspace(B, T, Rk, G))
-    return set_error(DYNCONV_ERR_WORKSPACE, "lr_fwd (tensor core): workspace too small");
-  return lr_tm_fwd_launch(x, z, U, sw, y, ws, B, T, D, G, R, Rk, W, residual, st);
-}
-
-int lr_tc_fwd_launch_lanes(const void* x, const void* z, const void* U, const void* sw, void* y, void* ws,
-                           size_t ws_bytes, int64_t B, int64_t T, int64_t D, int G, int R, int Rk, int W, int residual,
-                           cudaStream_t st) {
   if (!ws || ws_bytes < lr_tc_fwd_workspace(B, T, Rk, G))
     return set_error(DYNCONV_ERR_WORKSPACE, "lr_fwd (tensor core): workspace too small");
   const int rkp = (Rk + 15) / 16 * 16;

@@ -1,12 +1,11 @@
 // lowrank_tc.cuh -- pieces shared by the tcgen05 lowrank forward (lowrank_tc.cu)
-// and backward (lowrank_bwd_tc.cu) kernels, bf16 only.
+// and backward (lowrank_bwd_tm.cu) kernels, bf16 only.
 //
-// Work split: a tile is 128 channels (one channel block, the MMA M dimension)
-// x 64 timesteps of one batch row.  CTA (dblk, g) of a grid of n_dblk x n_groups
-// owns channel block dblk for the contiguous range of tiles [j0, j1) of group g,
-// tiles numbered b * tiles_row + t0 / 64.  A fixed channel block per CTA means
-// its U block is loaded once, and the CTAs of one tile (one per channel block)
-// run in step, which the backward's cross-CTA dz reduction relies on.
+// Forward work split: a tile is 128 channels (one channel block, the MMA M
+// dimension) x 64 timesteps of one batch row.  CTA (dblk, g) of a grid of
+// n_dblk x n_groups owns channel block dblk for the contiguous range of tiles
+// [j0, j1) of group g, tiles numbered b * tiles_row + t0 / 64, so its U block is
+// loaded once.  (The backward uses 128-step tiles; lowrank_bwd_tm.cu.)
 //
 // z_pack: z rows are 2R bytes (30 at R = 15), which TMA cannot tile (row pitch
 // not a multiple of 16 bytes), so z plus the static rank is first packed as
@@ -82,12 +81,6 @@ EncodeTiledFn encode_fn();
 int make_btd_map(CUtensorMap* map, const void* base, int64_t B, int64_t T, int64_t D, int box_d, int box_t,
                  int swizzle_bytes = 0);
 
-// 4-D bf16 map viewing a [B][T][D] tensor as [B][D/64][T][64] (D % 64 == 0):
-// dims (64, T, D/64, B), box (64, box_t, 2, 1), 128-byte swizzle.  One load then
-// brings 128 channels x box_t steps as two 64-channel swizzle atoms, box_t * 128
-// bytes apart -- the layout two 3-D loads of 64 channels would produce.
-int make_btd4_map(CUtensorMap* map, const void* base, int64_t B, int64_t T, int64_t D, int box_t);
-
 // 4-D bf16 map over z_pack [G*RKP/8][B][T][8]: dims (8, T, B, G*RKP/8), box (8, rows, 1,
 // RKP/8); group g's box starts at coordinate g*RKP/8 of the last dimension.  The box
 // lands as [RKP/8][rows][8] (16-byte rows, 8-rank chunks rows*16 bytes apart); rows
@@ -141,29 +134,6 @@ __device__ void load_u_block(uint8_t* us, const __nv_bfloat16* __restrict__ U, c
         *reinterpret_cast<__nv_bfloat16*>(us + w * kUTap + kmajor_off(v8 * 8 + k, r, kUSbo, 128)) = h[k];
     }
   }
-}
-
-// U^T into tensor memory as the K-major A operand of the weight MMAs: lane = channel,
-// column w*RKP/2 + c of the region holds ranks (2c, 2c+1) of tap w, read from the
-// K-major shared-memory copy (ranks 2c, 2c+1 are adjacent there, one 4-byte load
-// per TMEM word).  Called by one warp per TMEM lane quarter q.
-template <int W, int RKP>
-__device__ __forceinline__ void stage_ut_tmem(const uint8_t* us, uint32_t taddr_region, int q, int lane) {
-  constexpr uint32_t kUTap = (uint32_t)kBD * RKP * 2;
-  constexpr uint32_t kUChunk = (RKP / 8) * 128;
-  const int ch = q * 32 + lane;
-#pragma unroll
-  for (int w = 0; w < W; ++w) {
-#pragma unroll
-    for (int c0 = 0; c0 < RKP / 2; c0 += 8) {
-      uint32_t v[8];
-#pragma unroll
-      for (int i = 0; i < 8; ++i)
-        v[i] = *reinterpret_cast<const uint32_t*>(us + w * kUTap + kmajor_off(ch, 2 * (c0 + i), kUChunk, 128));
-      tmem_st8(taddr_region + ((uint32_t)(q * 32) << 16) + w * (RKP / 2) + c0, v);
-    }
-  }
-  tmem_st_wait();
 }
 
 }  // namespace lrtc
