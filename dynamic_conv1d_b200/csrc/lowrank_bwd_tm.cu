@@ -113,44 +113,6 @@ inline TmSplit tm_split(int64_t B, int64_t T, int64_t D) {
   return sp;
 }
 
-// U_ext block of channels [dlb, dlb + 128) of one group into shared memory as
-// 8 x 8 blocks [tap][ch/8][r/8][8 r][8 ch]: the MN-major B operand of the weight
-// MMA (N = channels, K = ranks) and the K-major B operand of the dz MMA (K =
-// channels of a tap, N = ranks) at once.  Rank R is static_w when given, zero up
-// to RKP; channels past Dg are zero.
-template <int W, int RKP, int NT>
-__device__ void load_u_tm(uint8_t* us, const __nv_bfloat16* __restrict__ U, const __nv_bfloat16* __restrict__ sw,
-                          int dlb, int Dg, int R, int tid) {
-  constexpr int NV = W * RKP * (kBD / 8);
-  constexpr int PER = (NV + NT - 1) / NT;
-  uint4 u[PER];
-#pragma unroll
-  for (int i = 0; i < PER; ++i) {
-    const int e = tid + i * NT;
-    u[i] = make_uint4(0, 0, 0, 0);
-    if (e < NV) {
-      const int c8 = e % (kBD / 8);
-      const int r = (e / (kBD / 8)) % RKP;
-      const int w = e / ((kBD / 8) * RKP);
-      const int d = dlb + 8 * c8;
-      if (d < Dg) {
-        if (r < R) u[i] = __ldg(reinterpret_cast<const uint4*>(U + ((size_t)r * W + w) * Dg + d));
-        else if (r == R && sw != nullptr) u[i] = __ldg(reinterpret_cast<const uint4*>(sw + (size_t)w * Dg + d));
-      }
-    }
-  }
-#pragma unroll
-  for (int i = 0; i < PER; ++i) {
-    const int e = tid + i * NT;
-    if (e < NV) {
-      const int c8 = e % (kBD / 8);
-      const int r = (e / (kBD / 8)) % RKP;
-      const int w = e / ((kBD / 8) * RKP);
-      *reinterpret_cast<uint4*>(us + ((w * 16 + c8) * (RKP / 8) + r / 8) * 128 + (r % 8) * 16) = u[i];
-    }
-  }
-}
-
 template <int W, int RKP>
 __global__ void __launch_bounds__(kThreads, 1)
     lr_bwd_tm_kernel(const __grid_constant__ CUtensorMap dymap, const __grid_constant__ CUtensorMap xmap,
@@ -218,7 +180,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint32_t tmem = 0;
   if (warp != 0) {
     constexpr int kNonProducer = kThreads - 32;
-    load_u_tm<W, RKP, kNonProducer>(smem + L::kOffU, U + (size_t)grp * R * W * cg.Dg,
+    load_u_mn<W, RKP, kNonProducer>(smem + L::kOffU, U + (size_t)grp * R * W * cg.Dg,
                                     sw ? sw + (size_t)grp * W * cg.Dg : nullptr, dl0, cg.Dg, R, threadIdx.x - 32);
     fence_proxy_async_smem();
     if (warp == 1) {

@@ -11,7 +11,7 @@
 //        (z_pack = z_ext as [R_kernel/8][B][T][8] bf16 with the static rank = 1.0,
 //         written once per call by z_pack_kernel; z rows are 2R bytes, which TMA
 //         cannot tile directly when R is odd)
-//   smem U (per 128-channel block, static_w folded as rank R)   [K-major, per tap]
+//   smem U (per 128-channel block, static_w folded as rank R)   [MN-major, per tap]
 //   tcgen05.mma (M = 128 channels, N = 64 timesteps, K = R_kernel) per tap w
 //        -> TMEM acc_w[ch][t] = sum_r U[r,w,ch] z[t,r]      (the dynamic weights;
 //                                                            never written to HBM)
@@ -154,8 +154,8 @@ struct FwdSmem {
   // K-major operand strides
   static constexpr uint32_t kZLbo = kBT * 16;          // next 8-rank chunk of z
   static constexpr uint32_t kZSbo = 128;               // next 8 timesteps
-  static constexpr uint32_t kULbo = 128;               // next 8-rank chunk of U
-  static constexpr uint32_t kUSbo = (RKP / 8) * 128;   // next 8 channels
+  static constexpr uint32_t kULbo = 128;               // U (MN-major): next 8-rank chunk
+  static constexpr uint32_t kUSbo = (RKP / 8) * 128;   // U (MN-major): next 8 channels
 };
 
 // ------------------------------------------------------------- forward kernel
@@ -206,9 +206,9 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
     // U block of this CTA's channels (MMA A operand), loaded once by all but the
     // producer, then the TMEM allocation.
     constexpr int kNonProducer = kFwdThreads - 32;
-    load_u_block<W, RKP, kNonProducer>(smem + L::kOffU, U + (size_t)grp * R * W * cg.Dg,
-                                       sw ? sw + (size_t)grp * W * cg.Dg : nullptr, dblk - grp * cg.nd, cg.Dg, R,
-                                       threadIdx.x - 32);
+    load_u_mn<W, RKP, kNonProducer>(smem + L::kOffU, U + (size_t)grp * R * W * cg.Dg,
+                                    sw ? sw + (size_t)grp * W * cg.Dg : nullptr, (dblk - grp * cg.nd) * kBD, cg.Dg, R,
+                                    threadIdx.x - 32);
     fence_proxy_async_smem();
     if (warp == 1) {
       tmem_alloc(&tmem_slot, kTmemCols);
@@ -236,7 +236,7 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
     __syncwarp();
   } else if (warp == 1) {
     // ------------------------------------------------------------ MMA issuer
-    const uint32_t idesc = make_idesc_bf16(kBD, kBT, 0, 0);
+    const uint32_t idesc = make_idesc_bf16(kBD, kBT, 1, 0);  // A = U^T (MN-major: channels), B = z (K-major)
     uint8_t* us = smem + L::kOffU;
     for (int k = 0; k < n; ++k) {
       const int s = k % S, a = k & 1;
@@ -294,13 +294,20 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
 #pragma unroll
           for (int j = 0; j < 16; ++j) xr[W - 1 + j] = __bfloat162float(xs[(tb + j + W - 1) * kBD + ch]);
           tmem_ld_wait();
+          // two steps at a time with packed f32x2 arithmetic (each lane rounds like the scalar op)
 #pragma unroll
-          for (int j = 0; j < 16; ++j) {
-            float yv = 0.f;
+          for (int j = 0; j < 16; j += 2) {
+            float2 y2 = mul2(make_float2(acc[0][j], acc[0][j + 1]), make_float2(xr[W - 1 + j], xr[W + j]));
 #pragma unroll
-            for (int w = 0; w < W; ++w) yv = fmaf(acc[w][j], xr[W - 1 + j - w], yv);
-            if (residual) yv += xr[W - 1 + j];
-            ys[(c * 16 + j) * 32 + lane] = __float2bfloat16_rn(yv);
+            for (int w = 1; w < W; ++w)
+              y2 = fma2(make_float2(acc[w][j], acc[w][j + 1]), make_float2(xr[W - 1 + j - w], xr[W + j - w]), y2);
+            if (residual) y2 = add2(y2, make_float2(xr[W - 1 + j], xr[W + j]));
+            // lane pairs swap halves so that each lane stores one whole 32-bit word: the even
+            // lane channels (l, l+1) of step j, the odd lane channels (l-1, l) of step j+1
+            const uint32_t mine = pack_bf16x2(y2.x, y2.y);  // (step j, step j+1) of channel `lane`
+            const uint32_t other = __shfl_xor_sync(0xffffffffu, mine, 1);
+            const uint32_t word = (lane & 1) ? __byte_perm(other, mine, 0x7632) : __byte_perm(mine, other, 0x5410);
+            *reinterpret_cast<uint32_t*>(ys + (c * 16 + j + (lane & 1)) * 32 + (lane & ~1)) = word;
           }
 #pragma unroll
           for (int j = 0; j < W - 1; ++j) xr[j] = xr[16 + j];

@@ -92,32 +92,30 @@ size_t zpack_bytes(int64_t B, int64_t T, int rkp, int G = 1);
 int z_pack_launch(const void* z, void* zp, int64_t B, int64_t T, int R, int rkp, bool has_static, cudaStream_t st,
                   int G = 1);
 
-// Loads U_ext for channel block dblk into shared memory: one [128 ch x RKP] K-major
-// no-swizzle block per tap (rank R = static_w when present, zero up to RKP).  The NT
-// calling threads each read up to ceil(W*RKP*16 / NT) 16-byte vectors (8 channels
-// of one (rank, tap) row; D % 8 == 0 on the tensor-core path, so a vector never
-// straddles the end of D), all loads issued before any store.
+// U_ext block of channels [dlb, dlb + 128) of one group into shared memory as 8 x 8
+// blocks [tap][ch/8][r/8][8 r][8 ch] (a 16-byte row = 8 channels of one rank): the
+// MN-major operand "M or N = channels, K = ranks" (sbo = (RKP/8) * 128 between
+// 8-channel groups, lbo = 128 between 8-rank groups), and also the K-major operand
+// "K = channels, N = ranks" of the backward's dz MMA.  Rank R is static_w when
+// given, zero up to RKP; channels past Dg are zero.  Consecutive threads fill
+// consecutive 16-byte rows (rank-fastest), so the stores are bank-conflict-free;
+// each thread issues all its 16-byte loads before its stores.
 template <int W, int RKP, int NT>
-__device__ void load_u_block(uint8_t* us, const __nv_bfloat16* __restrict__ U, const __nv_bfloat16* __restrict__ sw,
-                             int dblk, int D, int R, int tid) {
-  constexpr uint32_t kUTap = (uint32_t)kBD * RKP * 2;
-  constexpr uint32_t kUSbo = (RKP / 8) * 128;
+__device__ void load_u_mn(uint8_t* us, const __nv_bfloat16* __restrict__ U, const __nv_bfloat16* __restrict__ sw,
+                          int dlb, int Dg, int R, int tid) {
   constexpr int NV = W * RKP * (kBD / 8);
   constexpr int PER = (NV + NT - 1) / NT;
-  const int d0 = dblk * kBD;
   uint4 u[PER];
 #pragma unroll
   for (int i = 0; i < PER; ++i) {
     const int e = tid + i * NT;
     u[i] = make_uint4(0, 0, 0, 0);
     if (e < NV) {
-      const int v8 = e % (kBD / 8);  // 8-channel group
-      const int r = (e / (kBD / 8)) % RKP;
-      const int w = e / ((kBD / 8) * RKP);
-      const int d = d0 + v8 * 8;
-      if (d < D) {
-        if (r < R) u[i] = __ldg(reinterpret_cast<const uint4*>(U + ((size_t)r * W + w) * D + d));
-        else if (r == R && sw != nullptr) u[i] = __ldg(reinterpret_cast<const uint4*>(sw + (size_t)w * D + d));
+      const int r = e % RKP, c8 = (e / RKP) % (kBD / 8), w = e / (RKP * (kBD / 8));
+      const int d = dlb + 8 * c8;
+      if (d < Dg) {
+        if (r < R) u[i] = __ldg(reinterpret_cast<const uint4*>(U + ((size_t)r * W + w) * Dg + d));
+        else if (r == R && sw != nullptr) u[i] = __ldg(reinterpret_cast<const uint4*>(sw + (size_t)w * Dg + d));
       }
     }
   }
@@ -125,13 +123,8 @@ __device__ void load_u_block(uint8_t* us, const __nv_bfloat16* __restrict__ U, c
   for (int i = 0; i < PER; ++i) {
     const int e = tid + i * NT;
     if (e < NV) {
-      const int v8 = e % (kBD / 8);
-      const int r = (e / (kBD / 8)) % RKP;
-      const int w = e / ((kBD / 8) * RKP);
-      const __nv_bfloat16* h = reinterpret_cast<const __nv_bfloat16*>(&u[i]);
-#pragma unroll
-      for (int k = 0; k < 8; ++k)
-        *reinterpret_cast<__nv_bfloat16*>(us + w * kUTap + kmajor_off(v8 * 8 + k, r, kUSbo, 128)) = h[k];
+      const int r = e % RKP, c8 = (e / RKP) % (kBD / 8), w = e / (RKP * (kBD / 8));
+      *reinterpret_cast<uint4*>(us + ((w * 16 + c8) * (RKP / 8) + r / 8) * 128 + (r % 8) * 16) = u[i];
     }
   }
 }

@@ -47,6 +47,11 @@ CASES = {
     "sw128_transpose": (128, 16, 16, 16, 3, 1024, 2048, 0, 128, 256, 0),
     "sw128_K32": (128, 32, 32, 32, 3, 1024, 4096, 0, 128, 512, 0),
     "sw128_M64": (64, 16, 16, 16, 3, 1024, 2048, 0, 128, 256, 0),
+    # forward weight MMA: A = U^T MN-major (16-byte rows of 8 channels; 8-channel groups
+    # RKP/8 x 128 B apart, 8-rank groups 128 B apart), B = z K-major
+    "fwd_mnA_R16": (128, 64, 16, 64, 1, 256, 128, 0, 128, 64 * 16, 0),
+    "fwd_mnA_R32": (128, 64, 32, 64, 1, 512, 128, 0, 128, 64 * 16, 0),
+    "fwd_mnA_R64": (128, 64, 64, 64, 1, 1024, 128, 0, 128, 64 * 16, 0),
     # time-major backward (M = 128 timesteps): weight MMA, A = z rows t+w (K-major, rows
     # 16 B apart, 8-rank chunks 136 rows apart), B = U tap w (MN-major, N = 32 channels)
     "tm_w_R16": (128, 32, 16, 32, 0, 128, 136 * 16, 1, 256, 128, 0, 0),
