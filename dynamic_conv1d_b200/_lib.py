@@ -42,12 +42,13 @@ _SIGNATURES = {
     "dynconv_lr_fwd_grouped_workspace_bytes": (_c_size, [_c_i64] * 6 + [_c_int, _c_int]),
     "dynconv_lr_fwd_grouped": (_c_int, [_c_vp] * 5 + [_c_vp, _c_size] + [_c_i64] * 6 + [_c_int, _c_int, _c_vp]),
     "dynconv_lr_bwd_grouped_workspace_bytes": (_c_size, [_c_i64] * 6 + [_c_int, _c_int]),
-    "dynconv_lr_bwd_grouped": (_c_int, [_c_vp] * 10 + [_c_vp, _c_size] + [_c_i64] * 6 + [_c_int, _c_int, _c_vp]),
+    "dynconv_lr_bwd_grouped": (_c_int, [_c_vp] * 10 + [_c_vp, _c_size] + [_c_i64] * 6 + [_c_int, _c_int, _c_vp, _c_vp]),
     "dynconv_comm_blob_bytes": (_c_size, []),
     "dynconv_comm_create": (_c_int, [_c_int, _c_int, _c_i64, ctypes.POINTER(_c_vp), _c_vp]),
     "dynconv_comm_connect": (_c_int, [_c_vp, _c_vp]),
     "dynconv_comm_destroy": (_c_int, [_c_vp]),
-    "dynconv_lr_bwd_grouped_dp": (_c_int, [_c_vp] * 10 + [_c_vp, _c_size] + [_c_i64] * 6 + [_c_int, _c_int, _c_vp, _c_vp]),
+    "dynconv_lr_bwd_grouped_dp": (_c_int, [_c_vp] * 10 + [_c_vp, _c_size] + [_c_i64] * 6
+                                  + [_c_int, _c_int, _c_vp, _c_vp, _c_vp]),
     "dynconv_cast_f32": (_c_int, [_c_vp, _c_vp, _c_i64, _c_int, _c_vp]),
     "dynconv_umma_selftest": (_c_int, [_c_vp, _c_vp, _c_vp] + [_c_int] * 12 + [_c_vp]),
     "dynconv_wait_selftest": (_c_int, [ctypes.c_uint64, _c_vp, _c_vp]),

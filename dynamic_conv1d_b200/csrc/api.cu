@@ -120,10 +120,11 @@ int lr_tc_fwd_launch(const void* x, const void* z, const void* U, const void* sw
                      int64_t B, int64_t T, int64_t D, int G, int R, int Rk, int W, int residual, cudaStream_t st);
 int lr_tc_bwd_launch(const void* x, const void* z, const void* U, const void* sw, const void* dy, void* dx, void* dz,
                      float* dU_f32, void* dU, void* dsw, void* ws, size_t ws_bytes, int64_t B, int64_t T, int64_t D,
-                     int G, int R, int Rk, int W, int residual, cudaStream_t st);
+                     int G, int R, int Rk, int W, int residual, const void* zp, cudaStream_t st);
 int lr_tm_bwd_launch(const void* x, const void* z, const void* U, const void* sw, const void* dy, void* dx, void* dz,
                      float* dU_f32, void* dU, void* dsw, void* ws, size_t ws_bytes, int64_t B, int64_t T, int64_t D,
-                     int G, int R, int Rk, int W, int residual, const lrtc::DpPeers* peers, cudaStream_t st);
+                     int G, int R, int Rk, int W, int residual, const lrtc::DpPeers* peers, const void* zp,
+                     cudaStream_t st);
 bool comm_peers(const void* comm, lrtc::DpPeers* out);
 int comm_device(const void* comm);
 
@@ -367,7 +368,7 @@ static int cast_grouped(const float* dU_f32, void* dU, void* dsw, int64_t G, int
 int dynconv_lr_bwd_grouped(const void* x, const void* z, const void* U, const void* static_w, const void* dy,
                            void* dx, void* dz, void* dU, void* dstatic_w, float* dU_f32, void* workspace,
                            size_t workspace_bytes, int64_t B, int64_t T, int64_t D, int64_t R, int64_t W, int64_t G,
-                           int dtype, int residual, void* stream) {
+                           int dtype, int residual, const void* z_packed, void* stream) {
   int s;
   if ((s = lr_checks(B, T, D, R, W, dtype))) return s;
   if ((s = check_groups(G))) return s;
@@ -383,8 +384,8 @@ int dynconv_lr_bwd_grouped(const void* x, const void* z, const void* U, const vo
     return cast_grouped(dU_f32, dU, has_static ? dstatic_w : nullptr, G, R, Rk, W, D, dtype, st);
   }
   if (!x || !z || !U || !dy || !dx || !dz) return set_error(DYNCONV_ERR_ARGUMENT, "lr_bwd: null tensor");
-  const void* ptrs[] = {x, z, U, static_w, dy, dx, dz};
-  const bool tc = lr_tc_bwd_supported(D, Rk, (int)W, dtype, ptrs, 7, (int)G);
+  const void* ptrs[] = {x, z, U, static_w, dy, dx, dz, z_packed};
+  const bool tc = lr_tc_bwd_supported(D, Rk, (int)W, dtype, ptrs, 8, (int)G);
   if (!tc && G > 1)
     return set_error(DYNCONV_ERR_UNSUPPORTED,
                      "lr_bwd_grouped: G=%lld groups need the tensor-core path (bf16, W <= 4, R_kernel <= 32, "
@@ -395,7 +396,7 @@ int dynconv_lr_bwd_grouped(const void* x, const void* z, const void* U, const vo
     return set_error(DYNCONV_ERR_WORKSPACE, "lr_bwd: workspace %zu < %zu bytes", workspace_bytes, need);
   if (tc)
     return lr_tc_bwd_launch(x, z, U, static_w, dy, dx, dz, dU_f32, dU, dstatic_w, workspace, workspace_bytes, B, T, D,
-                            (int)G, (int)R, Rk, (int)W, residual, st);
+                            (int)G, (int)R, Rk, (int)W, residual, z_packed, st);
   float* part = (float*)workspace;
   if ((s = lr_bwd_simple_launch(x, z, U, static_w, dy, dx, dz, part, B, T, D, (int)R, Rk, (int)W, dtype, residual, st)))
     return s;
@@ -407,7 +408,7 @@ int dynconv_lr_bwd_grouped(const void* x, const void* z, const void* U, const vo
 int dynconv_lr_bwd_grouped_dp(const void* x, const void* z, const void* U, const void* static_w, const void* dy,
                               void* dx, void* dz, void* dU, void* dstatic_w, float* dU_f32, void* workspace,
                               size_t workspace_bytes, int64_t B, int64_t T, int64_t D, int64_t R, int64_t W, int64_t G,
-                              int dtype, int residual, void* comm, void* stream) {
+                              int dtype, int residual, const void* z_packed, void* comm, void* stream) {
   int s;
   if ((s = lr_checks(B, T, D, R, W, dtype))) return s;
   if ((s = check_groups(G))) return s;
@@ -421,8 +422,8 @@ int dynconv_lr_bwd_grouped_dp(const void* x, const void* z, const void* U, const
   if (cudaGetDevice(&dev) != cudaSuccess || dev != comm_device(comm))
     return set_error(DYNCONV_ERR_ARGUMENT, "lr_bwd_dp: the communicator belongs to device %d, current is %d",
                      comm_device(comm), dev);
-  const void* ptrs[] = {x, z, U, static_w, dy, dx, dz};
-  if (B * T == 0 || !lr_tc_bwd_supported(D, Rk, (int)W, dtype, ptrs, 7, (int)G))
+  const void* ptrs[] = {x, z, U, static_w, dy, dx, dz, z_packed};
+  if (B * T == 0 || !lr_tc_bwd_supported(D, Rk, (int)W, dtype, ptrs, 8, (int)G))
     return set_error(DYNCONV_ERR_UNSUPPORTED,
                      "lr_bwd_dp: the fused data-parallel backward needs the tensor-core path (bf16, W <= 4, "
                      "R_kernel <= 32, B*T > 0, 16-byte aligned tensors); all-reduce dU_f32 of dynconv_lr_bwd_grouped "
@@ -431,14 +432,14 @@ int dynconv_lr_bwd_grouped_dp(const void* x, const void* z, const void* U, const
   if (!workspace || workspace_bytes < need)
     return set_error(DYNCONV_ERR_WORKSPACE, "lr_bwd_dp: workspace %zu < %zu bytes", workspace_bytes, need);
   return lr_tm_bwd_launch(x, z, U, static_w, dy, dx, dz, dU_f32, dU, dstatic_w, workspace, workspace_bytes, B, T, D,
-                          (int)G, (int)R, Rk, (int)W, residual, &peers, (cudaStream_t)stream);
+                          (int)G, (int)R, Rk, (int)W, residual, &peers, z_packed, (cudaStream_t)stream);
 }
 
 int dynconv_lr_bwd(const void* x, const void* z, const void* U, const void* static_w, const void* dy, void* dx,
                    void* dz, void* dU, void* dstatic_w, float* dU_f32, void* workspace, size_t workspace_bytes,
                    int64_t B, int64_t T, int64_t D, int64_t R, int64_t W, int dtype, int residual, void* stream) {
   return dynconv_lr_bwd_grouped(x, z, U, static_w, dy, dx, dz, dU, dstatic_w, dU_f32, workspace, workspace_bytes, B,
-                                T, D, R, W, 1, dtype, residual, stream);
+                                T, D, R, W, 1, dtype, residual, nullptr, stream);
 }
 
 int dynconv_cast_f32(const float* src, void* dst, int64_t n, int dtype, void* stream) {

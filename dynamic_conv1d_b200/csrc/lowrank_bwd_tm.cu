@@ -491,34 +491,48 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
   }
 
-  // ---------------------------------------------------------------- dz reduction
-  // Publish this CTA's dz partials (CTA barrier, then one cumulative gpu-scope
-  // fence), wait for the other channel-block CTAs of the token group (co-resident:
-  // cooperative launch), then sum this CTA's share of the group's (step, channel
-  // group) pairs in channel-block order: deterministic, evenly spread.
+  // ---------------------------------------------------------------- tail
+  // Publish this CTA's dz and dU partials (CTA barrier, then one cumulative gpu-scope
+  // fence) on two counters: its token group's and the grid's.  Single rank: wait for
+  // the group's other channel-block CTAs (co-resident: cooperative launch), reduce dz,
+  // then wait for the grid and reduce dU.  Data parallel: wait for the grid at once,
+  // reduce dU and post this rank's sums to every peer, reduce dz while they travel,
+  // and only then wait for the peers' sums.
+  const bool dp = peers.world > 1;
+  const int par = (int)(dp_epoch & 1);
   tc_fence_before();
   __syncthreads();
   if (threadIdx.x == 0) {
     __threadfence();
     atomicAdd(&grp_done[g], 1);
-    atomicAdd(&grp_done[sp.n_groups], 1);  // grid-wide count, waited on before the dU reduction
-    bool ok = !abort_flag;
-    if (ok) {
-      const volatile int* gd = grp_done + g;
-      const uint64_t tstart = globaltimer_ns();
-      while (*gd < sp.n_dblk) {
-        if (globaltimer_ns() - tstart > kWaitLimitNs) {
-          atomicCAS(&g_device_error, 0u, (unsigned)kErrWaitTail);
-          ok = false;
-          break;
+    atomicAdd(&grp_done[sp.n_groups], 1);
+    grp_ok = abort_flag ? 0 : 1;
+  }
+  // bounded wait (thread 0) until *cnt reaches target; grp_ok = 0 on time-out
+  auto wait_count = [&](const int* cnt, int target) {
+    if (threadIdx.x == 0) {
+      bool ok = grp_ok != 0;
+      if (ok) {
+        const volatile int* c = cnt;
+        const uint64_t tstart = globaltimer_ns();
+        while (*c < target) {
+          if (globaltimer_ns() - tstart > kWaitLimitNs) {
+            atomicCAS(&g_device_error, 0u, (unsigned)kErrWaitTail);
+            ok = false;
+            break;
+          }
         }
       }
+      __threadfence();
+      grp_ok = ok ? 1 : 0;
     }
-    __threadfence();
-    grp_ok = ok ? 1 : 0;
-  }
-  __syncthreads();
-  if (grp_ok) {
+    __syncthreads();
+  };
+
+  // dz: this CTA's share of the group's (step, channel group) pairs, summed over the
+  // channel blocks in order: deterministic, evenly spread
+  auto dz_reduce = [&]() {
+    if (!grp_ok) return;
     const int64_t npairs = (int64_t)n * kTT * cg.G;
     const int64_t lo = npairs * dblk / sp.n_dblk, hi = npairs * (dblk + 1) / sp.n_dblk;
     constexpr int RQ = RKP / 4;  // float4 groups per step
@@ -548,31 +562,17 @@ __global__ void __launch_bounds__(kThreads, 1)
       for (int c = 0; c < 4; ++c)
         if (4 * rq + c < R) dst[4 * rq + c] = __float2bfloat16_rn(av[c]);
     }
-  }
+  };
 
-  // ---------------------------------------------------------------- dU reduction
-  // Once the whole grid has published its dU partial (the grid-wide count above),
-  // CTA i sums its 1/grid slice of the [G][Rk][W*Dg] accumulator over the token
+  if (!dp) {
+    wait_count(grp_done + g, sp.n_dblk);
+    dz_reduce();
+  }
+  wait_count(grp_done + sp.n_groups, (int)gridDim.x);
+
+  // dU: CTA i sums its 1/grid slice of the [G][Rk][W*Dg] accumulator over the token
   // groups in group order (deterministic) and writes dU_f32, and the bf16 dU rows /
   // dstatic_w rows when they are requested.
-  __syncthreads();
-  if (threadIdx.x == 0) {
-    bool ok = grp_ok != 0;
-    if (ok) {
-      const volatile int* gd = grp_done + sp.n_groups;
-      const uint64_t tstart = globaltimer_ns();
-      while (*gd < (int)gridDim.x) {
-        if (globaltimer_ns() - tstart > kWaitLimitNs) {
-          atomicCAS(&g_device_error, 0u, (unsigned)kErrWaitTail);
-          ok = false;
-          break;
-        }
-      }
-    }
-    __threadfence();
-    grp_ok = ok ? 1 : 0;
-  }
-  __syncthreads();
   const int64_t wd = (int64_t)W * cg.Dg;
   const int64_t per_g = (int64_t)Rk * wd;  // one group's [Rk][W*Dg] block
   const int64_t n4 = cg.G * per_g / 4;     // W*Dg % 4 == 0 (Dg % 8 == 0)
@@ -594,8 +594,6 @@ __global__ void __launch_bounds__(kThreads, 1)
       dst[3] = __float2bfloat16_rn(a4.w);
     }
   };
-  const bool dp = peers.world > 1;
-  const int par = (int)(dp_epoch & 1);
   if (grp_ok) {
     for (int64_t i = lo + threadIdx.x; i < hi; i += blockDim.x) {
       float4 a4 = make_float4(0.f, 0.f, 0.f, 0.f);
@@ -619,18 +617,20 @@ __global__ void __launch_bounds__(kThreads, 1)
   if (dp) {
     // Publish: every thread's peer stores, then one system-scope fence per thread,
     // the CTA barrier, and this CTA's count of float4s added to every rank's counter
-    // for this source.  Then wait until every source has delivered all n4 float4s of
-    // this call (counters are cumulative: this call completes at the delivered total
-    // before it plus n4) and sum
-    // the world sources in rank order -- the same order on every rank, so all ranks
-    // hold bit-identical results.
+    // for this source.  While the stores travel, reduce dz (the grid-wide wait above
+    // covers the token group's).  Then wait until every source has delivered all n4
+    // float4s of this call (counters are cumulative: this call completes at the
+    // delivered total before it plus n4) and sum the world sources in rank order --
+    // the same order on every rank, so all ranks hold bit-identical results.
     __threadfence_system();
+    __syncthreads();
+    if (threadIdx.x == 0 && grp_ok)
+      for (int p2 = 0; p2 < peers.world; ++p2)
+        atomicAdd_system(peers.flags[p2] + peers.rank, (unsigned long long)(hi - lo));
+    dz_reduce();
     __syncthreads();
     if (threadIdx.x == 0) {
       bool ok = grp_ok != 0;
-      if (ok)
-        for (int p2 = 0; p2 < peers.world; ++p2)
-          atomicAdd_system(peers.flags[p2] + peers.rank, (unsigned long long)(hi - lo));
       const unsigned long long target = dp_base + (unsigned long long)n4;
       const uint64_t tstart = globaltimer_ns();
       for (int src = 0; ok && src < peers.world; ++src) {
@@ -707,7 +707,7 @@ TmWorkspace tm_workspace(void* base, int64_t B, int64_t T, int64_t D, int Rk, in
 template <int W, int RKP>
 int launch_tm(const void* x, const void* z, const void* U, const void* sw, const void* dy, void* dx, void* dz,
               float* dU_f32, void* dU, void* dsw, void* wsp, int64_t B, int64_t T, int64_t D, int G, int R, int Rk,
-              int residual, const DpPeers& peers, cudaStream_t st) {
+              int residual, const DpPeers& peers, const void* zp_in, cudaStream_t st) {
   using L = TmCfg<W, RKP>;
   CUtensorMap dymap, xmap, zmap;
   int s;
@@ -719,8 +719,10 @@ int launch_tm(const void* x, const void* z, const void* U, const void* sw, const
   if ((s = make_btd_map(&xmap, x, B, T, Dt, 64, kRowsXY, 128))) return s;
   CUtensorMap dxmap;
   if ((s = make_btd_map(&dxmap, dx, B, T, Dt, 16, 32, 32))) return s;  // per-warp [32 steps][16 ch] stores
-  if ((s = make_zpack_map(&zmap, ws.zp, B, T, RKP, kZR, G))) return s;
-  if ((s = z_pack_launch(z, ws.zp, B, T, R, RKP, sw != nullptr, st, G))) return s;
+  // z packed by the forward (same z) is read as it is; otherwise pack it here
+  const void* zp = zp_in ? zp_in : ws.zp;
+  if ((s = make_zpack_map(&zmap, zp, B, T, RKP, kZR, G))) return s;
+  if (!zp_in && (s = z_pack_launch(z, ws.zp, B, T, R, RKP, sw != nullptr, st, G))) return s;
   cudaError_t e = cudaMemsetAsync(ws.cnt, 0, (size_t)(sp.n_groups + 1) * sizeof(int), st);
   if (e != cudaSuccess) return cuda_status(e, "cudaMemsetAsync(group counters)");
   const int smem = (int)L::kTotal;
@@ -757,12 +759,12 @@ int launch_tm(const void* x, const void* z, const void* U, const void* sw, const
 template <int RKP>
 int launch_tm_w(int W, const void* x, const void* z, const void* U, const void* sw, const void* dy, void* dx,
                 void* dz, float* dU_f32, void* dU, void* dsw, void* ws, int64_t B, int64_t T, int64_t D, int G, int R,
-                int Rk, int residual, const DpPeers& pr, cudaStream_t st) {
+                int Rk, int residual, const DpPeers& pr, const void* zp, cudaStream_t st) {
   switch (W) {
-    case 1: return launch_tm<1, RKP>(x, z, U, sw, dy, dx, dz, dU_f32, dU, dsw, ws, B, T, D, G, R, Rk, residual, pr, st);
-    case 2: return launch_tm<2, RKP>(x, z, U, sw, dy, dx, dz, dU_f32, dU, dsw, ws, B, T, D, G, R, Rk, residual, pr, st);
-    case 3: return launch_tm<3, RKP>(x, z, U, sw, dy, dx, dz, dU_f32, dU, dsw, ws, B, T, D, G, R, Rk, residual, pr, st);
-    case 4: return launch_tm<4, RKP>(x, z, U, sw, dy, dx, dz, dU_f32, dU, dsw, ws, B, T, D, G, R, Rk, residual, pr, st);
+    case 1: return launch_tm<1, RKP>(x, z, U, sw, dy, dx, dz, dU_f32, dU, dsw, ws, B, T, D, G, R, Rk, residual, pr, zp, st);
+    case 2: return launch_tm<2, RKP>(x, z, U, sw, dy, dx, dz, dU_f32, dU, dsw, ws, B, T, D, G, R, Rk, residual, pr, zp, st);
+    case 3: return launch_tm<3, RKP>(x, z, U, sw, dy, dx, dz, dU_f32, dU, dsw, ws, B, T, D, G, R, Rk, residual, pr, zp, st);
+    case 4: return launch_tm<4, RKP>(x, z, U, sw, dy, dx, dz, dU_f32, dU, dsw, ws, B, T, D, G, R, Rk, residual, pr, zp, st);
     default: return set_error(DYNCONV_ERR_UNSUPPORTED, "tensor-core backward: W=%d", W);
   }
 }
@@ -791,10 +793,12 @@ size_t lr_tc_bwd_workspace(int64_t B, int64_t T, int64_t D, int Rk, int W, int G
 }
 
 // peers == nullptr: single-GPU result.  Otherwise dU_f32 / dU / dstatic_w receive the
-// sum over the peers' ranks, reduced inside the kernel over peer memory.
+// sum over the peers' ranks, reduced inside the kernel over peer memory.  zp: z already
+// packed by the forward ([G*RKP/8][B][T][8]), or nullptr to pack it here.
 int lr_tm_bwd_launch(const void* x, const void* z, const void* U, const void* sw, const void* dy, void* dx, void* dz,
                      float* dU_f32, void* dU, void* dsw, void* ws, size_t ws_bytes, int64_t B, int64_t T, int64_t D,
-                     int G, int R, int Rk, int W, int residual, const DpPeers* peers, cudaStream_t st) {
+                     int G, int R, int Rk, int W, int residual, const DpPeers* peers, const void* zp,
+                     cudaStream_t st) {
   if (ws_bytes < lr_tm_bwd_workspace(B, T, D, Rk, W, G))
     return set_error(DYNCONV_ERR_WORKSPACE, "lr_bwd (tensor core): workspace too small");
   DpPeers pr = {};
@@ -806,15 +810,15 @@ int lr_tm_bwd_launch(const void* x, const void* z, const void* U, const void* sw
                        (long long)pr.cap, (long long)((int64_t)G * Rk * W * D));
   }
   if (Rk <= 16)
-    return launch_tm_w<16>(W, x, z, U, sw, dy, dx, dz, dU_f32, dU, dsw, ws, B, T, D, G, R, Rk, residual, pr, st);
-  return launch_tm_w<32>(W, x, z, U, sw, dy, dx, dz, dU_f32, dU, dsw, ws, B, T, D, G, R, Rk, residual, pr, st);
+    return launch_tm_w<16>(W, x, z, U, sw, dy, dx, dz, dU_f32, dU, dsw, ws, B, T, D, G, R, Rk, residual, pr, zp, st);
+  return launch_tm_w<32>(W, x, z, U, sw, dy, dx, dz, dU_f32, dU, dsw, ws, B, T, D, G, R, Rk, residual, pr, zp, st);
 }
 
 int lr_tc_bwd_launch(const void* x, const void* z, const void* U, const void* sw, const void* dy, void* dx, void* dz,
                      float* dU_f32, void* dU, void* dsw, void* ws, size_t ws_bytes, int64_t B, int64_t T, int64_t D,
-                     int G, int R, int Rk, int W, int residual, cudaStream_t st) {
+                     int G, int R, int Rk, int W, int residual, const void* zp, cudaStream_t st) {
   return lr_tm_bwd_launch(x, z, U, sw, dy, dx, dz, dU_f32, dU, dsw, ws, ws_bytes, B, T, D, G, R, Rk, W, residual,
-                          nullptr, st);
+                          nullptr, zp, st);
 }
 
 }  // namespace dynconv

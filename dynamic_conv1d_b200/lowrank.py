@@ -25,7 +25,7 @@ from .parallel import allreduce_shared_grad, comm_for, current_group
 
 
 def _fused_dp_backward(lib, group, x, z, U, static_w, dy, dx, dz, dU_f32, ws, B, T, D, R, W, G, code, residual,
-                       stream):
+                       zpack, stream):
     """The backward with the sum over data-parallel ranks done inside the kernel
     (dynconv_lr_bwd_grouped_dp).  Returns (dU [G*R, W*D], dstatic_w [G, W*D] or None),
     bf16, already summed over the ranks; None when the fused path does not apply
@@ -47,7 +47,7 @@ def _fused_dp_backward(lib, group, x, z, U, static_w, dy, dx, dz, dU_f32, ws, B,
     status = lib.dynconv_lr_bwd_grouped_dp(
         _lib.ptr(x), _lib.ptr(z), _lib.ptr(U), _lib.ptr(static_w), _lib.ptr(dy),
         _lib.ptr(dx), _lib.ptr(dz), _lib.ptr(dU), _lib.ptr(dsw), _lib.ptr(dU_f32),
-        _lib.ptr(ws), ws.numel(), B, T, D, R, W, G, code, int(residual), comm.ptr, stream,
+        _lib.ptr(ws), ws.numel(), B, T, D, R, W, G, code, int(residual), _lib.ptr(zpack), comm.ptr, stream,
     )
     # Every rank is now committed to the in-kernel exchange: a rank-local refusal (an
     # unaligned tensor, an empty shard) is an error, not a silent switch to NCCL that
@@ -84,6 +84,7 @@ class _LowrankDynamicConvolutionFn(torch.autograd.Function):
         )
         _lib.after_call(y)
         ctx.save_for_backward(x, z_k, U_k, sw_k)
+        ctx.zpack = ws if nbytes > 0 else None  # z packed for the tensor cores, reused by the backward
         ctx.dtypes = (z.dtype, U.dtype, None if static_w is None else static_w.dtype)
         ctx.residual = bool(residual)
         ctx.group = current_group()
@@ -113,7 +114,7 @@ class _LowrankDynamicConvolutionFn(torch.autograd.Function):
         fused = None
         if reduce_first:
             fused = _fused_dp_backward(lib, ctx.group, x, z, U, static_w, dy, dx, dz, dU_f32, ws,
-                                       B, T, D, R, W, 1, code, ctx.residual, stream)
+                                       B, T, D, R, W, 1, code, ctx.residual, ctx.zpack, stream)
         if fused is not None:
             reduce_first = False  # summed over the ranks and cast inside the kernel
             dU = fused[0]
@@ -122,11 +123,11 @@ class _LowrankDynamicConvolutionFn(torch.autograd.Function):
             dU = None if reduce_first else torch.empty_like(U)
             dsw = None if (reduce_first or not has_static) else torch.empty((W, D), device=x.device, dtype=x.dtype)
             _lib.check(
-                lib.dynconv_lr_bwd(
+                lib.dynconv_lr_bwd_grouped(
                     _lib.ptr(x), _lib.ptr(z), _lib.ptr(U), _lib.ptr(static_w), _lib.ptr(dy),
                     _lib.ptr(dx), _lib.ptr(dz), _lib.ptr(dU), _lib.ptr(dsw), _lib.ptr(dU_f32),
                     _lib.ptr(ws), ws.numel(),
-                    B, T, D, R, W, code, int(ctx.residual), stream,
+                    B, T, D, R, W, 1, code, int(ctx.residual), _lib.ptr(ctx.zpack), stream,
                 )
             )
         if reduce_first:
@@ -216,6 +217,7 @@ class _LowrankGroupedFn(torch.autograd.Function):
         )
         _lib.after_call(y)
         ctx.save_for_backward(x, z, U, static_w)
+        ctx.zpack = ws if nbytes > 0 else None  # z packed for the tensor cores, reused by the backward
         ctx.residual = bool(residual)
         ctx.group = current_group()
         return y
@@ -244,7 +246,7 @@ class _LowrankGroupedFn(torch.autograd.Function):
         reduce_first = ctx.group is not None
         if reduce_first:
             fused = _fused_dp_backward(lib, ctx.group, x, z, U, static_w, dy, dx, dz, dU_f32, ws,
-                                       B, T, D, R, W, G, code, ctx.residual, stream)
+                                       B, T, D, R, W, G, code, ctx.residual, ctx.zpack, stream)
             if fused is not None:
                 _lib.after_call(dx)
                 dsw = fused[1].view(G, W, D) if has_static else None
@@ -256,7 +258,7 @@ class _LowrankGroupedFn(torch.autograd.Function):
                 _lib.ptr(x), _lib.ptr(z), _lib.ptr(U), _lib.ptr(static_w), _lib.ptr(dy),
                 _lib.ptr(dx), _lib.ptr(dz), _lib.ptr(dU), _lib.ptr(dsw), _lib.ptr(dU_f32),
                 _lib.ptr(ws), ws.numel(),
-                B, T, D, R, W, G, code, int(ctx.residual), stream,
+                B, T, D, R, W, G, code, int(ctx.residual), _lib.ptr(ctx.zpack), stream,
             )
         )
         if reduce_first:

@@ -53,6 +53,19 @@ def data_parallel(group=None):
         _state.group = prev
 
 
+@contextlib.contextmanager
+def local_gradients():
+    """Within this context the ops reduce nothing, even inside ``data_parallel``: the
+    caller sums the shared gradients itself (``sequence_parallel`` does, once for its
+    two calls)."""
+    prev = getattr(_state, "group", None)
+    _state.group = None
+    try:
+        yield
+    finally:
+        _state.group = prev
+
+
 class _Comm:
     """The library's data-parallel communicator for one (process group, device): peer
     landing buffers mapped over CUDA IPC, used by the fused lowrank backward

@@ -3,15 +3,14 @@ ranks, and each rank exchanges a (W-1)-row halo with its neighbours.
 
 Output step t depends on x at steps t-W+1 .. t only (causal, reference.py:5-39),
 so a rank that holds steps [t0, t1) of every sequence needs just the W-1 rows of x
-before t0, held by the previous rank.  The forward prepends them (zeros on rank 0,
-where they are the sequence's own zero padding), runs the op on the extended
-slice and drops the W-1 extra outputs.  In the backward, the gradient that falls
-on the borrowed rows is sent back to the previous rank and added to the
-gradient of its last W-1 rows.  The mixing weights (z, or the headwise weights)
-are needed at the local steps only; the borrowed rows get zero weights, and
-their outputs are discarded.  The shared parameters' gradients (U, static_w) are
-partial sums over the local steps and are all-reduced through
-``data_parallel(group)``, as for batch sharding.
+before t0, held by the previous rank (on rank 0 they are the sequence's own zero
+padding).  The op runs on the local slice unchanged, and a second call on a
+2(W-1)-row window supplies the terms of the borrowed rows (``sequence_parallel``
+below), so nothing of the size of the slice is copied.  In the backward, the
+gradient that falls on the borrowed rows is sent back to the previous rank and
+added to the gradient of its last W-1 rows.  The shared parameters' gradients
+(U, static_w) are partial sums over the local steps; they are summed over the
+ranks by one all-reduce, as for batch sharding.
 
 Every rank must hold at least W-1 steps.  Ranks are ordered along time by
 their rank in ``group``."""
@@ -22,7 +21,7 @@ import torch.distributed as dist
 
 from .headwise import headwise_dynamic_convolution
 from .lowrank import lowrank_dynamic_convolution
-from .parallel import data_parallel
+from .parallel import local_gradients
 
 
 def _peer(group, r: int) -> int:
@@ -56,58 +55,143 @@ def _check_lengths(T: int, h: int, device, group) -> None:
                          f"the shortest slice holds {t_min} (this rank {T})")
 
 
-class _HaloPrepend(torch.autograd.Function):
-    """[B, T, D] -> [B, h + T, D]: the previous rank's last h rows, then the local rows."""
+class _SPEnter(torch.autograd.Function):
+    """Splits the inputs of one sequence-parallel call into the main call's inputs
+    (views of the local tensors) and the halo correction's inputs, and does in its
+    backward every exchange the call needs, in one fixed order on every rank: the
+    halo gradient back to the previous rank, then one all-reduce of the shared
+    gradients.
+
+    Correction inputs, each 2h rows long: x_s = [the previous rank's last h rows of x,
+    h zero rows], mix_s = [h zero rows, the first h local rows of mix]."""
 
     @staticmethod
-    def forward(ctx, x, h, group):
+    def forward(ctx, h, group, x, mix, *params):
         world = dist.get_world_size(group)
         rank = dist.get_rank(group)
         B, T = x.shape[0], x.shape[1]
         _check_lengths(T, h, x.device, group)
-        send = x[:, T - h:].contiguous()
-        halo = _exchange(send, rank + 1 if rank + 1 < world else None, (B, h) + tuple(x.shape[2:]),
-                         rank - 1 if rank > 0 else None, x, group)
+        has_prev, has_next = rank > 0, rank + 1 < world
+        send = x[:, T - h:].contiguous() if has_next else None
+        halo = _exchange(send, rank + 1 if has_next else None, (B, h) + tuple(x.shape[2:]),
+                         rank - 1 if has_prev else None, x, group)
         ctx.h, ctx.group, ctx.T = h, group, T
-        return torch.cat([halo, x], dim=1)
+        ctx.has_prev, ctx.has_next = has_prev, has_next
+        ctx.x_meta = (x.shape, x.dtype, x.device)
+        x_s = torch.zeros((B, 2 * h) + tuple(x.shape[2:]), dtype=x.dtype, device=x.device)
+        x_s[:, :h] = halo
+        mix_s = torch.zeros((B, 2 * h) + tuple(mix.shape[2:]), dtype=mix.dtype, device=mix.device)
+        mix_s[:, h:] = mix[:, :h]
+        return (x.view_as(x), mix.view_as(mix), x_s, mix_s) + tuple(p.view_as(p) for p in params)
+
+    @staticmethod
+    def backward(ctx, g_x, g_mix, g_xs, g_mixs, *g_params):
+        h, group, T = ctx.h, ctx.group, ctx.T
+        rank = dist.get_rank(group)
+        shape, dtype, device = ctx.x_meta
+        halo_shape = (shape[0], h) + tuple(shape[2:])
+        # the gradient of the borrowed rows goes back to their owner, the previous rank
+        # (sent even when it is zero: the owner posts the matching receive)
+        send = None
+        if ctx.has_prev:
+            send = (g_xs[:, :h].contiguous() if g_xs is not None
+                    else torch.zeros(halo_shape, dtype=dtype, device=device))
+        back = _exchange(send, rank - 1 if ctx.has_prev else None, halo_shape,
+                         rank + 1 if ctx.has_next else None, torch.empty(0, dtype=dtype, device=device), group)
+        # g_x / g_mix are the main call's fresh gradient buffers (one consumer each):
+        # the h-row fix-ups are added in place
+        if ctx.has_next and g_x is not None:
+            g_x[:, T - h:] += back
+        if g_mixs is not None and g_mix is not None:
+            g_mix[:, :h] += g_mixs[:, h:]
+        return (None, None, g_x, g_mix) + _sum_shared(list(g_params), group)
+
+
+def _sum_shared(grads, group) -> tuple:
+    """One SUM all-reduce of the shared parameters' gradients over the ranks (float32,
+    packed into one buffer), cast back to each parameter's dtype."""
+    live = [g for g in grads if g is not None]
+    if not live or dist.get_world_size(group) == 1:
+        return tuple(grads)
+    flat = torch.cat([g.reshape(-1).float() for g in live])
+    dist.all_reduce(flat, op=dist.ReduceOp.SUM, group=group)
+    out, i = [], 0
+    for g in grads:
+        if g is None:
+            out.append(None)
+            continue
+        out.append(flat[i:i + g.numel()].view(g.shape).to(g.dtype))
+        i += g.numel()
+    return tuple(out)
+
+
+class _SharedSum(torch.autograd.Function):
+    """Identity on the shared parameters; their gradients are summed over the ranks
+    (W = 1: no halo, nothing else to exchange)."""
+
+    @staticmethod
+    def forward(ctx, group, *params):
+        ctx.group = group
+        return tuple(p.view_as(p) for p in params)
+
+    @staticmethod
+    def backward(ctx, *grads):
+        return (None,) + _sum_shared(list(grads), ctx.group)
+
+
+class _SPExit(torch.autograd.Function):
+    """y[:, :h] += the halo correction's last h output rows (in place on the main
+    call's output)."""
+
+    @staticmethod
+    def forward(ctx, y, y_s, h):
+        y[:, :h] += y_s[:, h:]
+        ctx.mark_dirty(y)
+        ctx.h = h
+        return y
 
     @staticmethod
     def backward(ctx, g):
-        h, group, T = ctx.h, ctx.group, ctx.T
-        world = dist.get_world_size(group)
-        rank = dist.get_rank(group)
-        g = g.contiguous()
-        g_halo = g[:, :h].contiguous()
-        back = _exchange(g_halo, rank - 1 if rank > 0 else None, g_halo.shape, rank + 1 if rank + 1 < world else None,
-                         g, group)
-        g_local = g[:, h:].clone()
-        if rank + 1 < world:
-            g_local[:, T - h:] += back
-        return g_local, None, None
-
-
-def _zero_rows_front(t: torch.Tensor, h: int) -> torch.Tensor:
-    pad = torch.zeros((t.shape[0], h) + tuple(t.shape[2:]), dtype=t.dtype, device=t.device)
-    return torch.cat([pad, t], dim=1)
+        h = ctx.h
+        g_s = torch.zeros((g.shape[0], 2 * h) + tuple(g.shape[2:]), dtype=g.dtype, device=g.device)
+        g_s[:, h:] = g[:, :h]
+        return g, g_s, None
 
 
 def sequence_parallel(fn, x, mix, *params, residual: bool = False, W: int, group=None):
-    """Runs ``fn(x_ext, mix_ext, *params, residual=...)`` on this rank's time slice.
+    """Runs ``fn(x, mix, *params, residual=...)`` on this rank's time slice.
 
     ``mix`` is the per-step mixing input (lowrank z [B, T, R], headwise weight
     [B, T, H, W]); ``params`` are the shared parameters.  Returns the local
     output [B, T, D]; gradients flow to x, mix and params, with the shared ones
-    all-reduced over ``group``."""
+    summed over ``group``.
+
+    ``fn`` runs on the local slice as it is -- its first W-1 outputs then miss the
+    terms of the previous rank's rows, which the causal window reads as zero padding --
+    and once more on a 2(W-1)-row window (the borrowed rows, then zeros as x; zeros,
+    then the first W-1 local rows as mix, without the residual).  The op is linear in
+    x for fixed mixing weights, so that window's last W-1 outputs are exactly the
+    missing terms, and they are added to the first W-1 outputs.  No copy of the
+    local slice is made; the extra traffic is O(W) rows per sequence.  Rank 0 has
+    no previous rank and skips the window."""
     group = group if group is not None else dist.group.WORLD
     h = W - 1
+    live = [p for p in params if p is not None]
     if h == 0:
-        with data_parallel(group):
-            return fn(x, mix, *params, residual=residual)
-    x_ext = _HaloPrepend.apply(x, h, group)
-    mix_ext = _zero_rows_front(mix, h)
-    with data_parallel(group):
-        y_ext = fn(x_ext.contiguous(), mix_ext.contiguous(), *params, residual=residual)
-    return y_ext[:, h:]
+        live_v = list(_SharedSum.apply(group, *live)) if live else []
+    else:
+        x, mix, x_s, mix_s, *live_v = _SPEnter.apply(h, group, x, mix, *live)
+    it = iter(live_v)
+    params_v = [None if p is None else next(it) for p in params]
+    # the shared gradients are summed once, by _SPEnter's (or _SharedSum's) backward, not by fn
+    with local_gradients():
+        y = fn(x, mix, *params_v, residual=residual)
+        if h == 0:
+            return y
+        if dist.get_rank(group) > 0:
+            y_s = fn(x_s, mix_s, *params_v, residual=False)
+            y = _SPExit.apply(y, y_s, h)
+    return y
 
 
 def lowrank_dynamic_convolution_sp(x, z, U, static_w=None, residual: bool = False, group=None):

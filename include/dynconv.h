@@ -189,11 +189,15 @@ int dynconv_lr_fwd_grouped(const void* x, const void* z, const void* U, const vo
                            int dtype, int residual, void* stream);
 size_t dynconv_lr_bwd_grouped_workspace_bytes(int64_t B, int64_t T, int64_t D, int64_t R, int64_t W, int64_t G,
                                               int dtype, int has_static);
+/* z_packed: NULL, or the workspace of the dynconv_lr_fwd_grouped call that produced y from
+ * this same z (same B, T, R, G and static_w presence, z unchanged since): on the tensor-core
+ * path that workspace holds z packed for the MMAs, and the backward reads it instead of
+ * packing z again (one launch fewer).  16-byte aligned. */
 int dynconv_lr_bwd_grouped(const void* x, const void* z, const void* U, const void* static_w, const void* dy,
                            void* dx, void* dz, void* dU, void* dstatic_w, float* dU_f32,
                            void* workspace, size_t workspace_bytes,
                            int64_t B, int64_t T, int64_t D, int64_t R, int64_t W, int64_t G,
-                           int dtype, int residual, void* stream);
+                           int dtype, int residual, const void* z_packed, void* stream);
 
 /* ------------------------------------------- data parallel (fused all-reduce) */
 
@@ -226,7 +230,7 @@ int dynconv_lr_bwd_grouped_dp(const void* x, const void* z, const void* U, const
                               void* dx, void* dz, void* dU, void* dstatic_w, float* dU_f32,
                               void* workspace, size_t workspace_bytes,
                               int64_t B, int64_t T, int64_t D, int64_t R, int64_t W, int64_t G,
-                              int dtype, int residual, void* comm, void* stream);
+                              int dtype, int residual, const void* z_packed, void* comm, void* stream);
 
 /* dst[i] = (dtype) src[i], i < n, round-to-nearest-even.  Used after the
  * data-parallel all-reduce of the float32 shared-gradient buffers (replaces

@@ -77,9 +77,7 @@ def _worker(rank, world, port, W, q, kind="lowrank"):
         sh = [p.clone().requires_grad_() for p in shared]
         y = sequence_parallel(fn, xl, zl, *sh, residual=True, W=W)
         y.backward(dy[:, lo:hi])
-        # the torch stand-in does not all-reduce its shared gradients; do it here
-        for p in sh:
-            dist.all_reduce(p.grad)
+        # the shared gradients come back already summed over the ranks
         q.put((rank, lo, hi, y.detach(), xl.grad, zl.grad) + tuple(p.grad for p in sh))
         dist.barrier()
         dist.destroy_process_group()
