@@ -1,20 +1,22 @@
 // dp_comm.cu -- the data-parallel communicator of the fused lowrank backward.
 //
 // Each rank (one process per GPU on one node) allocates, once, a landing buffer
-// [2 parities][world sources][cap floats] and a flag array [world sources] of
-// 64-bit counters in its own device memory, exports CUDA IPC handles of both,
-// and opens every peer's handles.  The backward kernel (lowrank_bwd_tm.cu) then
-// writes this rank's dU / dstatic_w sum straight into slot [parity][rank] of every
-// rank's landing buffer over NVLink (plain stores to peer memory), counts the
-// float4s it delivered on each rank's counter for this source, waits (bounded)
-// until every source has delivered the whole buffer, and sums the world slots in
-// rank order -- so all ranks hold the same, deterministic result, and the
-// all-reduce replaces the NCCL collective that followed the kernel.  Only plain
-// stores, loads and atomics touch peer memory (no TMA, no switch-side reduction).
+// [2 parities][world sources][cap floats] and a flag array [world sources][kMaxDpCtas]
+// of 64-bit call numbers in its own device memory, exports CUDA IPC handles of both,
+// and opens every peer's handles.  In the backward kernel (lowrank_bwd_tm.cu) CTA i
+// of every rank owns the same slice of the dU / dstatic_w buffer: it writes this
+// rank's sum of its slice straight into slot [parity][rank] of every rank's landing
+// buffer over NVLink (plain stores to peer memory), then stores the call number in
+// flag [rank][i] of every rank, waits (bounded) until flag [src][i] of its own array
+// shows the call for every source, and sums the world slots of its slice in rank
+// order -- so all ranks hold the same, deterministic result, and the all-reduce
+// replaces the NCCL collective that followed the kernel.  Each flag has one writer,
+// so no CTA waits on another CTA's slice and no flag is contended.  Only plain
+// stores and loads touch peer memory (no TMA, no switch-side reduction).
 //
-// The counters are cumulative, and the call count and the delivered total live on
-// the device (advanced by the kernel), so calls may differ in size and the kernels
-// can be captured in a CUDA graph and replayed.
+// The flags hold call numbers, and the call count lives on the device (advanced by
+// the kernel), so calls may differ in size and the kernels can be captured in a
+// CUDA graph and replayed.
 // Landing slots alternate by call parity: a rank can only be two calls ahead of a
 // peer once that peer has finished reading the older call's slot (a call's
 // kernel waits for every peer's contribution to that call).
@@ -31,8 +33,8 @@ struct Comm {
   int world = 0, rank = 0, device = -1;
   int64_t cap = 0;             // floats per (parity, source) slot
   float* land = nullptr;       // own landing buffer
-  unsigned long long* flags = nullptr;  // own counters [world]
-  unsigned long long* epoch = nullptr;  // own [calls completed, float4s delivered per source]
+  unsigned long long* flags = nullptr;  // own flags [world][kMaxDpCtas]
+  unsigned long long* epoch = nullptr;  // own count of completed calls
   bool connected = false;
   float* peer_land[lrtc::kMaxWorld] = {};
   unsigned long long* peer_flags[lrtc::kMaxWorld] = {};
@@ -91,9 +93,10 @@ int dynconv_comm_create(int world, int rank, int64_t max_floats, void** comm, vo
   c->cap = max_floats;
   cudaError_t e = cudaGetDevice(&c->device);
   if (e == cudaSuccess) e = cudaMalloc(&c->land, (size_t)2 * world * max_floats * sizeof(float));
-  if (e == cudaSuccess) e = cudaMalloc(&c->flags, (size_t)(world + 2) * sizeof(unsigned long long));
-  if (e == cudaSuccess) e = cudaMemset(c->flags, 0, (size_t)(world + 2) * sizeof(unsigned long long));
-  if (e == cudaSuccess) c->epoch = c->flags + world;
+  const size_t nflags = (size_t)world * lrtc::kMaxDpCtas + 1;  // + the call counter
+  if (e == cudaSuccess) e = cudaMalloc(&c->flags, nflags * sizeof(unsigned long long));
+  if (e == cudaSuccess) e = cudaMemset(c->flags, 0, nflags * sizeof(unsigned long long));
+  if (e == cudaSuccess) c->epoch = c->flags + (size_t)world * lrtc::kMaxDpCtas;
   Blob b;
   memset(&b, 0, sizeof(b));
   if (e == cudaSuccess) e = cudaIpcGetMemHandle(&b.land, c->land);

@@ -132,7 +132,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   __shared__ uint32_t tmem_slot;
   __shared__ int abort_flag;
   __shared__ int grp_ok;
-  __shared__ unsigned long long dp_epoch_s, dp_base_s;
+  __shared__ unsigned long long dp_epoch_s;
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int dblk = blockIdx.x % sp.n_dblk;
@@ -165,8 +165,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     abort_flag = 0;
     // data-parallel call counter and the float4s each source has delivered so far (calls
     // may differ in size); read before any CTA of this launch advances them
-    dp_epoch_s = peers.world > 1 ? reinterpret_cast<volatile unsigned long long*>(peers.epoch)[0] : 0ull;
-    dp_base_s = peers.world > 1 ? reinterpret_cast<volatile unsigned long long*>(peers.epoch)[1] : 0ull;
+    dp_epoch_s = peers.world > 1 ? *reinterpret_cast<volatile unsigned long long*>(peers.epoch) : 0ull;
     fence_barrier_init();
   }
   if (warp == 0 && lane == 0) {
@@ -176,7 +175,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     prefetch_tensormap(&dxmap);
   }
   __syncthreads();  // barriers initialised: the producer starts its loads at once
-  const unsigned long long dp_epoch = dp_epoch_s, dp_base = dp_base_s;
+  const unsigned long long dp_epoch = dp_epoch_s;
   uint32_t tmem = 0;
   if (warp != 0) {
     constexpr int kNonProducer = kThreads - 32;
@@ -616,26 +615,26 @@ __global__ void __launch_bounds__(kThreads, 1)
   }
   if (dp) {
     // Publish: every thread's peer stores, then one system-scope fence per thread,
-    // the CTA barrier, and this CTA's count of float4s added to every rank's counter
-    // for this source.  While the stores travel, reduce dz (the grid-wide wait above
-    // covers the token group's).  Then wait until every source has delivered all n4
-    // float4s of this call (counters are cumulative: this call completes at the
-    // delivered total before it plus n4) and sum the world sources in rank order --
-    // the same order on every rank, so all ranks hold bit-identical results.
+    // the CTA barrier, and this call's number in flag [rank][this CTA] of every rank.
+    // While the stores travel, reduce dz (the grid-wide wait above covers the token
+    // group's).  Then wait until flag [src][this CTA] shows this call for every
+    // source -- CTA i of every rank owns the same slice [lo, hi) -- and sum the world
+    // sources in rank order: the same order on every rank, so all ranks hold
+    // bit-identical results.
+    const unsigned long long call = dp_epoch + 1;
     __threadfence_system();
     __syncthreads();
     if (threadIdx.x == 0 && grp_ok)
       for (int p2 = 0; p2 < peers.world; ++p2)
-        atomicAdd_system(peers.flags[p2] + peers.rank, (unsigned long long)(hi - lo));
+        reinterpret_cast<volatile unsigned long long*>(peers.flags[p2])[peers.rank * kMaxDpCtas + blockIdx.x] = call;
     dz_reduce();
     __syncthreads();
     if (threadIdx.x == 0) {
       bool ok = grp_ok != 0;
-      const unsigned long long target = dp_base + (unsigned long long)n4;
       const uint64_t tstart = globaltimer_ns();
       for (int src = 0; ok && src < peers.world; ++src) {
-        const volatile unsigned long long* f = peers.flags[peers.rank] + src;
-        while (*f < target) {
+        const volatile unsigned long long* f = peers.flags[peers.rank] + src * kMaxDpCtas + blockIdx.x;
+        while (*f < call) {
           if (globaltimer_ns() - tstart > kWaitLimitNs) {
             atomicCAS(&g_device_error, 0u, (unsigned)kErrWaitTail);
             ok = false;
@@ -660,11 +659,8 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         finish(i, a4);
       }
-      // one CTA advances the counters; every CTA of this launch read them at the start
-      if (blockIdx.x == 0 && threadIdx.x == 0) {
-        peers.epoch[0] = dp_epoch + 1;
-        peers.epoch[1] = dp_base + (unsigned long long)n4;
-      }
+      // one CTA advances the call count; every CTA of this launch read it at the start
+      if (blockIdx.x == 0 && threadIdx.x == 0) *peers.epoch = call;
     }
   }
   tc_fence_before();
@@ -734,6 +730,8 @@ int launch_tm(const void* x, const void* z, const void* U, const void* sw, const
   // Cooperative launch: the CTAs of a token group wait for one another before
   // the dz reduction, so the whole grid must be co-resident (grid <= SM count,
   // one CTA per SM; lr_tc_bwd_supported checks the first bound).
+  if (peers.world > 1 && sp.n_dblk * sp.n_groups > kMaxDpCtas)  // one flag per CTA and source
+    return set_error(DYNCONV_ERR_UNSUPPORTED, "lr_bwd_dp: grid of %d CTAs > %d", sp.n_dblk * sp.n_groups, kMaxDpCtas);
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3((unsigned)(sp.n_dblk * sp.n_groups));
   cfg.blockDim = dim3(kThreads);

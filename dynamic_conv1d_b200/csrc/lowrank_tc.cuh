@@ -51,16 +51,18 @@ struct ChanGroups {
 inline ChanGroups chan_groups(int64_t D, int G) { return ChanGroups{G, (int)((D + kBD - 1) / kBD), (int)D}; }
 
 // Data-parallel peers of the fused backward (dp_comm.cu): every rank's landing
-// buffer [2 parities][world sources][cap floats] and flag counters [world sources]
-// mapped into this process (peer memory over NVLink, plain loads and stores), and
-// this rank's device-side call counter.  world == 1: no cross-GPU reduction.
+// buffer [2 parities][world sources][cap floats] and flags [world sources][kMaxDpCtas]
+// (one per source CTA: the last call that CTA delivered its slice for) mapped into
+// this process (peer memory over NVLink, plain loads and stores), and this rank's
+// device-side call counter.  world == 1: no cross-GPU reduction.
 constexpr int kMaxWorld = 8;
+constexpr int kMaxDpCtas = 256;  // the backward's grid is at most one CTA per SM
 struct DpPeers {
   int world, rank;
   int64_t cap;                                   // floats per (parity, source) slot
   float* land[kMaxWorld];                        // rank p's landing buffer
-  unsigned long long* flags[kMaxWorld];          // rank p's per-source float4 counters
-  unsigned long long* epoch;                     // this rank's [calls completed, float4s per source so far]
+  unsigned long long* flags[kMaxWorld];          // rank p's flags [source][CTA]
+  unsigned long long* epoch;                     // this rank's count of completed calls
 };
 
 __host__ __device__ constexpr uint32_t round1024(uint32_t v) { return (v + 1023u) / 1024u * 1024u; }

@@ -207,7 +207,7 @@ int dynconv_lr_bwd_grouped(const void* x, const void* z, const void* U, const vo
  * shared-gradient buffer that the reference's caller would run after backward.
  *   1. dynconv_comm_create(world, rank, max_floats, &comm, blob) on each rank, with
  *      that rank's GPU current: allocates this rank's landing buffer
- *      (2 x world x max_floats floats) and counters, and writes a blob of
+ *      (2 x world x max_floats floats) and flags, and writes a blob of
  *      dynconv_comm_blob_bytes() bytes (CUDA IPC handles, device UUID, rank);
  *   2. exchange the blobs (any host channel, e.g. torch.distributed), in rank order;
  *   3. dynconv_comm_connect(comm, blobs) on each rank: maps every peer's buffers
