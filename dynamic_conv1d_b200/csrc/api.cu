@@ -2,7 +2,8 @@
 //
 // Validates shapes, pointers and dtypes, carves the caller's workspace, and
 // dispatches to the kernels.  It never allocates device memory and never
-// synchronises (except dynconv_check_device, whose job is to synchronise).
+// synchronises (except dynconv_check_device, whose job is to synchronise, and the
+// one-time set-up of the host-visible error word on a device's first call).
 #include <atomic>
 #include <mutex>
 #include <stdarg.h>
@@ -18,6 +19,11 @@ namespace {
 thread_local char g_last_error[512] = "";
 std::atomic<uint64_t> g_launches{0};
 }  // namespace
+
+thread_local int t_no_alloc_scope = 0;
+
+NoAllocScope::NoAllocScope() { ++t_no_alloc_scope; }
+NoAllocScope::~NoAllocScope() { --t_no_alloc_scope; }
 
 void note_launch(int n) { g_launches.fetch_add((uint64_t)n, std::memory_order_relaxed); }
 
@@ -86,13 +92,17 @@ int sm_count() {
 unsigned int lr_tc_error_word();
 unsigned int lr_bwd_tm_error_word();
 unsigned int hw_tma_error_word();
+unsigned int selftest_error_word();
+int lr_tc_error_word_wire(unsigned int* host_word);
+int lr_bwd_tm_error_word_wire(unsigned int* host_word);
+int hw_tma_error_word_wire(unsigned int* host_word);
+int selftest_error_word_wire(unsigned int* host_word);
 bool hw_tma_supported(int64_t D, int64_t H, int W, int log2hs, int dtype, const void* const* ptrs, int nptrs);
 int hw_tma_partial_rows(int64_t B, int64_t T, int64_t D, int log2hs);
 int hw_tma_fwd_launch(const void* x, const void* w, const void* sw, void* y, int64_t B, int64_t T, int64_t D, int64_t H,
                       int W, int log2hs, int residual, cudaStream_t st);
 int hw_tma_bwd_launch(const void* x, const void* w, const void* sw, const void* dy, void* dx, void* dw, float* part,
                       int64_t B, int64_t T, int64_t D, int64_t H, int W, int log2hs, int residual, cudaStream_t st);
-unsigned int selftest_error_word();
 int wait_selftest_launch(uint64_t limit_ns, int* out, cudaStream_t st);
 
 // kernels (other translation units)
@@ -148,6 +158,92 @@ int check_common(int64_t B, int64_t T, int64_t D, int64_t W) {
   return DYNCONV_OK;
 }
 
+// ---------------------------------------------------------------- host-visible error word
+// A kernel whose bounded wait gives up returns early and leaves its outputs
+// incomplete.  Besides the device word that dynconv_check_device reads, it stores the
+// wait site into this device's word of a small pinned, mapped host array, so the next
+// call of this library on the device sees it without synchronising and returns
+// DYNCONV_ERR_TIMEOUT.  The array is allocated, and every module's copy of the pointer
+// set, on the device's first kernel-launching call that is not being captured into a
+// CUDA graph (it synchronises once); until then only dynconv_check_device reports.
+
+constexpr int kMaxDevices = 64;
+std::mutex g_wire_mutex;
+std::atomic<unsigned int*> g_host_words{nullptr};  // [kMaxDevices], pinned and mapped
+std::atomic<int> g_wired[kMaxDevices];
+
+bool capturing(cudaStream_t st) {
+  cudaStreamCaptureStatus cs = cudaStreamCaptureStatusNone;
+  if (cudaStreamIsCapturing(st, &cs) != cudaSuccess) {
+    cudaGetLastError();
+    return true;  // unknown: treat as capturing (no synchronous calls)
+  }
+  return cs != cudaStreamCaptureStatusNone;
+}
+
+void wire_host_error_word(cudaStream_t st) {
+  if (t_no_alloc_scope) return;  // the no-allocation entry point allocates nothing, not even this
+  int dev = -1;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) return;
+  if (g_wired[dev].load(std::memory_order_acquire)) return;
+  if (capturing(st)) return;
+  std::lock_guard<std::mutex> lock(g_wire_mutex);
+  if (g_wired[dev].load(std::memory_order_relaxed)) return;
+  unsigned int* words = g_host_words.load(std::memory_order_acquire);
+  if (!words) {
+    void* p = nullptr;
+    if (cudaHostAlloc(&p, kMaxDevices * sizeof(unsigned int), cudaHostAllocMapped | cudaHostAllocPortable) !=
+        cudaSuccess) {
+      cudaGetLastError();
+      return;
+    }
+    memset(p, 0, kMaxDevices * sizeof(unsigned int));
+    words = static_cast<unsigned int*>(p);
+    g_host_words.store(words, std::memory_order_release);
+  }
+  void* dp = nullptr;
+  if (cudaHostGetDevicePointer(&dp, words, 0) != cudaSuccess || !dp) {
+    cudaGetLastError();
+    return;
+  }
+  unsigned int* mine = static_cast<unsigned int*>(dp) + dev;
+  if (lr_tc_error_word_wire(mine) || lr_bwd_tm_error_word_wire(mine) || hw_tma_error_word_wire(mine) ||
+      selftest_error_word_wire(mine)) {
+    cudaGetLastError();
+    return;
+  }
+  g_wired[dev].store(1, std::memory_order_release);
+}
+
+// DYNCONV_ERR_TIMEOUT if a kernel launched earlier on the current device gave up a
+// wait since the last report (reported once; the device words of the same event are
+// read and cleared here too, unless the stream is being captured).
+int report_earlier_timeout(cudaStream_t st) {
+  unsigned int* words = g_host_words.load(std::memory_order_acquire);
+  if (!words) return DYNCONV_OK;
+  int dev = -1;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) return DYNCONV_OK;
+  if (*reinterpret_cast<volatile unsigned int*>(words + dev) == 0) return DYNCONV_OK;
+  const unsigned int site = __atomic_exchange_n(words + dev, 0u, __ATOMIC_ACQ_REL);
+  if (site == 0) return DYNCONV_OK;
+  if (!capturing(st)) {
+    (void)lr_tc_error_word();
+    (void)lr_bwd_tm_error_word();
+    (void)selftest_error_word();
+    (void)hw_tma_error_word();
+  }
+  return set_error(DYNCONV_ERR_TIMEOUT,
+                   "a kernel launched earlier on device %d gave up a bounded wait (site %u): the outputs of that "
+                   "call are incomplete",
+                   dev, site);
+}
+
+// First step of every kernel-launching entry point.
+int op_entry(cudaStream_t st) {
+  wire_host_error_word(st);
+  return report_earlier_timeout(st);
+}
+
 int log2_exact(int64_t v) {
   int l = 0;
   while ((int64_t(1) << l) < v) ++l;
@@ -185,6 +281,13 @@ int dynconv_check_device(void* stream) {
   cudaStream_t st = (cudaStream_t)stream;
   cudaError_t e = cudaStreamSynchronize(st);
   if (e != cudaSuccess) return cuda_status(e, "cudaStreamSynchronize");
+  // the host-visible word holds the same events: cleared here, so the next call does
+  // not report them again
+  if (unsigned int* words = g_host_words.load(std::memory_order_acquire)) {
+    int dev = -1;
+    if (cudaGetDevice(&dev) == cudaSuccess && dev >= 0 && dev < kMaxDevices)
+      __atomic_exchange_n(words + dev, 0u, __ATOMIC_ACQ_REL);
+  }
   // every word is read (and so cleared) before the first non-zero one is reported
   const unsigned int words[4] = {lr_tc_error_word(), lr_bwd_tm_error_word(), selftest_error_word(),
                                  hw_tma_error_word()};
@@ -201,6 +304,7 @@ int dynconv_check_device(void* stream) {
 int dynconv_hw_fwd(const void* x, const void* weight, const void* static_w, void* y, int64_t B, int64_t T, int64_t D,
                    int64_t H, int64_t W, int dtype, int residual, void* stream) {
   int s;
+  if ((s = op_entry((cudaStream_t)stream))) return s;
   if ((s = check_dtype(dtype))) return s;
   if ((s = check_common(B, T, D, W))) return s;
   if (H <= 0 || D % H != 0) return set_error(DYNCONV_ERR_SHAPE, "D=%lld must be divisible by H=%lld", (long long)D, (long long)H);
@@ -232,6 +336,7 @@ int dynconv_hw_bwd(const void* x, const void* weight, const void* static_w, cons
                    void* dstatic_w, float* dstatic_w_f32, void* workspace, size_t workspace_bytes, int64_t B,
                    int64_t T, int64_t D, int64_t H, int64_t W, int dtype, int residual, void* stream) {
   int s;
+  if ((s = op_entry((cudaStream_t)stream))) return s;
   if ((s = check_dtype(dtype))) return s;
   if ((s = check_common(B, T, D, W))) return s;
   if (H <= 0 || D % H != 0) return set_error(DYNCONV_ERR_SHAPE, "D=%lld must be divisible by H=%lld", (long long)D, (long long)H);
@@ -302,6 +407,7 @@ int dynconv_lr_fwd_grouped(const void* x, const void* z, const void* U, const vo
                            void* workspace, size_t workspace_bytes, int64_t B, int64_t T, int64_t D, int64_t R,
                            int64_t W, int64_t G, int dtype, int residual, void* stream) {
   int s;
+  if ((s = op_entry((cudaStream_t)stream))) return s;
   if ((s = lr_checks(B, T, D, R, W, dtype))) return s;
   if ((s = check_groups(G))) return s;
   const int Rk = (int)R + (static_w ? 1 : 0);
@@ -370,6 +476,7 @@ int dynconv_lr_bwd_grouped(const void* x, const void* z, const void* U, const vo
                            size_t workspace_bytes, int64_t B, int64_t T, int64_t D, int64_t R, int64_t W, int64_t G,
                            int dtype, int residual, const void* z_packed, void* stream) {
   int s;
+  if ((s = op_entry((cudaStream_t)stream))) return s;
   if ((s = lr_checks(B, T, D, R, W, dtype))) return s;
   if ((s = check_groups(G))) return s;
   const bool has_static = static_w != nullptr;
@@ -410,6 +517,7 @@ int dynconv_lr_bwd_grouped_dp(const void* x, const void* z, const void* U, const
                               size_t workspace_bytes, int64_t B, int64_t T, int64_t D, int64_t R, int64_t W, int64_t G,
                               int dtype, int residual, const void* z_packed, void* comm, void* stream) {
   int s;
+  if ((s = op_entry((cudaStream_t)stream))) return s;
   if ((s = lr_checks(B, T, D, R, W, dtype))) return s;
   if ((s = check_groups(G))) return s;
   const bool has_static = static_w != nullptr;
@@ -444,6 +552,7 @@ int dynconv_lr_bwd(const void* x, const void* z, const void* U, const void* stat
 
 int dynconv_cast_f32(const float* src, void* dst, int64_t n, int dtype, void* stream) {
   int s;
+  if ((s = op_entry((cudaStream_t)stream))) return s;
   if ((s = check_dtype(dtype))) return s;
   if (n < 0) return set_error(DYNCONV_ERR_SHAPE, "n < 0");
   if (n > 0 && (!src || !dst)) return set_error(DYNCONV_ERR_ARGUMENT, "cast: null pointer");
@@ -462,6 +571,7 @@ int dynconv_wait_selftest(uint64_t limit_ns, int* out, void* stream) {
   if (limit_ns == 0 || limit_ns > 100000000ull)
     return set_error(DYNCONV_ERR_ARGUMENT, "wait_selftest: limit %llu ns outside 1 ns .. 100 ms",
                      (unsigned long long)limit_ns);
+  wire_host_error_word((cudaStream_t)stream);
   return wait_selftest_launch(limit_ns, out, (cudaStream_t)stream);
 }
 

@@ -23,6 +23,14 @@ namespace dynconv {
 
 // Records `msg` as the calling thread's last error and returns `status`.
 int set_error(int status, const char* fmt, ...);
+// While one exists on the calling thread, the library allocates nothing of its own
+// (the no-allocation entry point holds one around its call).
+struct NoAllocScope {
+  NoAllocScope();
+  ~NoAllocScope();
+  NoAllocScope(const NoAllocScope&) = delete;
+  NoAllocScope& operator=(const NoAllocScope&) = delete;
+};
 // Wraps a CUDA runtime status: DYNCONV_OK or DYNCONV_ERR_CUDA with the CUDA message.
 int cuda_status(cudaError_t e, const char* what);
 // Number of SMs of the current device (cached per device).
@@ -59,6 +67,24 @@ void note_launch(int n = 1);
 // dynconv_check_device() polls.
 static __device__ unsigned int g_device_error;
 
+// Host-visible copy of the error word: this device's word in pinned, mapped host
+// memory, which the host reads at the next library call without synchronising (the
+// call then reports DYNCONV_ERR_TIMEOUT).  The host wires it once per device (the
+// accessor's _wire function); until then it is null and only g_device_error is set.
+static __device__ unsigned int* g_host_error;
+
+// Records that a bounded wait gave up at `site`: the device word (first site wins)
+// and, once wired, the host-visible word (a plain store over the bus, then a system
+// fence; any nonzero site will do, so racing writers need no atomics).
+__device__ __forceinline__ void record_device_error(unsigned int site) {
+  atomicCAS(&g_device_error, 0u, site);
+  unsigned int* h = g_host_error;
+  if (h) {
+    *reinterpret_cast<volatile unsigned int*>(h) = site;
+    __threadfence_system();
+  }
+}
+
 #define DYNCONV_DEFINE_ERROR_ACCESSOR(fn)                                      \
   unsigned int fn() {                                                          \
     unsigned int v = 0;                                                        \
@@ -69,6 +95,12 @@ static __device__ unsigned int g_device_error;
       cudaMemcpyToSymbol(g_device_error, &z, sizeof(z));                       \
     }                                                                          \
     return v;                                                                  \
+  }                                                                            \
+  int fn##_wire(unsigned int* host_word) {                                     \
+    return cudaMemcpyToSymbol(g_host_error, &host_word, sizeof(host_word)) ==  \
+                   cudaSuccess                                                 \
+               ? 0                                                             \
+               : -1;                                                           \
   }
 
 enum DeviceErrorSite : unsigned int {
@@ -281,7 +313,7 @@ static __device__ __noinline__ bool mbar_wait_slow(uint64_t* bar, uint32_t parit
     if (*abort_flag) return false;
     if (globaltimer_ns() - t0 > limit_ns) break;
   }
-  atomicCAS(&g_device_error, 0u, site);
+  record_device_error(site);
   *abort_flag = 1;
   return false;
 }

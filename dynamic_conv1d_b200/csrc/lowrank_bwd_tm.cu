@@ -516,7 +516,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         const uint64_t tstart = globaltimer_ns();
         while (*c < target) {
           if (globaltimer_ns() - tstart > kWaitLimitNs) {
-            atomicCAS(&g_device_error, 0u, (unsigned)kErrWaitTail);
+            record_device_error(kErrWaitTail);
             ok = false;
             break;
           }
@@ -636,7 +636,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         const volatile unsigned long long* f = peers.flags[peers.rank] + src * kMaxDpCtas + blockIdx.x;
         while (*f < call) {
           if (globaltimer_ns() - tstart > kWaitLimitNs) {
-            atomicCAS(&g_device_error, 0u, (unsigned)kErrWaitTail);
+            record_device_error(kErrWaitTail);
             ok = false;
             break;
           }

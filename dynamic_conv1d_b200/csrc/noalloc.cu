@@ -70,5 +70,6 @@ extern "C" int dynconv_lr_fwd_noalloc(const void* x, const void* z, const void* 
   void* scratch = nullptr;
   int s = scratch_for_current_device(&scratch);
   if (s) return s;
+  const dynconv::NoAllocScope no_alloc;  // no pinned error-word array either
   return dynconv_lr_fwd(x, z, U, static_w, y, scratch, kScratchBytes, B, T, D, R, W, dtype, residual, stream);
 }

@@ -22,9 +22,18 @@
  *     state below (the noalloc scratch address, cached SM counts) all belong to
  *     the primary context.
  *   - Errors on the device: the tensor-core kernels bound every wait (1.5 s).  A
- *     wait that gives up makes its kernel return early and sets a device error
- *     word; the call itself has already returned DYNCONV_OK, so check once per
- *     step with dynconv_check_device (it synchronises the stream).
+ *     wait that gives up makes its kernel return early, leaving that call's
+ *     outputs incomplete, and sets a device error word; the call itself has
+ *     already returned DYNCONV_OK.  It is reported in two ways: (1) the next
+ *     kernel-launching call on the same device that starts after the kernel gave
+ *     up returns DYNCONV_ERR_TIMEOUT without launching anything (it reads a word
+ *     of pinned, mapped host memory that the kernel also wrote; no
+ *     synchronisation), once; (2) dynconv_check_device synchronises the stream
+ *     and reports it.  Use (2) once per step to learn of it before the outputs
+ *     are used.  The pinned word is set up on a device's first kernel-launching
+ *     call that is not being captured into a CUDA graph (that call synchronises
+ *     once); before that only (2) reports.  dynconv_lr_fwd_noalloc never sets
+ *     it up (it allocates nothing), but reports through it once it exists.
  */
 #ifndef DYNCONV_H_
 #define DYNCONV_H_
@@ -65,8 +74,9 @@ int dynconv_abi_version(void);
 const char* dynconv_status_string(int status);
 const char* dynconv_last_error(void);
 /* Synchronises `stream`, then reads and clears the device error word that
- * bounded waits inside the tensor-core kernels set when they give up.
- * Returns DYNCONV_OK, DYNCONV_ERR_TIMEOUT or DYNCONV_ERR_CUDA. */
+ * bounded waits inside the tensor-core kernels set when they give up (and the
+ * pinned host-visible copy of it, so the next call does not report the same
+ * event).  Returns DYNCONV_OK, DYNCONV_ERR_TIMEOUT or DYNCONV_ERR_CUDA. */
 int dynconv_check_device(void* stream);
 /* Number of kernels this library has launched in this process (all devices,
  * all threads).  Diagnostic only; no reference counterpart. */

@@ -3,8 +3,9 @@
 A one-CTA kernel waits on an mbarrier that nothing ever arrives on, through the
 same out-of-line bounded-wait code the tensor-core kernels use, with a 2 ms
 limit.  The wait gives up, the kernel returns, and the host sees
-DYNCONV_ERR_TIMEOUT from dynconv_check_device() (and from the op in debug mode)
--- with the CUDA context still usable: the next op runs and matches the oracle.
+DYNCONV_ERR_TIMEOUT from dynconv_check_device(), from the next op call (which
+reads the pinned host-visible error word), and from the op in debug mode -- with
+the CUDA context still usable: the next op runs and matches the oracle.
 No GPU fault, trap or hang is involved: the kernel simply exits early."""
 from __future__ import annotations
 
@@ -67,6 +68,25 @@ def test_wait_gives_up_and_reports_timeout():
     # the context is intact: a real op runs and matches the oracle
     _check_small_lowrank()
     assert lib.dynconv_check_device(_stream()) == 0
+
+
+def test_next_call_reports_timeout_without_check_device():
+    """A kernel that gave up a wait is reported by the next op call itself (the host
+    reads the pinned error word, no synchronisation), once; then calls run normally."""
+    torch.cuda.synchronize()
+    check_device(torch.empty(1, device="cuda"))  # start clean
+    x, z, U, sw = (t.cuda() for t in _small_lowrank())
+    lowrank_dynamic_convolution(x, z, U, sw, residual=True)  # this device's error word is wired
+    out = torch.zeros(1, dtype=torch.int32, device="cuda")
+    _run_wait(out)
+    torch.cuda.synchronize()  # the self-test kernel has finished; no check_device
+    with pytest.raises(DynconvError) as ei:
+        lowrank_dynamic_convolution(x, z, U, sw, residual=True)
+    assert ei.value.status == DYNCONV_ERR_TIMEOUT
+    assert "earlier" in str(ei.value)
+    # reported once, device words cleared with it: the next call runs and check_device is clean
+    _check_small_lowrank()
+    check_device(out)
 
 
 def test_check_device_raises():
