@@ -56,6 +56,10 @@ WORKLOADS = {
     # configs[1], configs[2]
     "headwise_hs32": dict(kind="headwise", B=4, T=4096, D=2048, H=64, W=4, static=True, residual=True),
     "headwise_hs1": dict(kind="headwise", B=4, T=4096, D=2048, H=2048, W=4, static=True, residual=True),
+    # shapes the reference accepts outside the tensor-core envelope (not BASELINE configs; run only
+    # with --workload): the cfg4 workload with W = 8 taps, and with rank 63 + static (R_kernel = 64)
+    "lowrank_w8": dict(kind="lowrank", B=4, T=4096, D=2048, R=15, W=8, static=True, residual=True),
+    "lowrank_r63": dict(kind="lowrank", B=4, T=4096, D=2048, R=63, W=4, static=True, residual=True),
 }
 
 

@@ -48,7 +48,7 @@ constexpr int kSmemCap = 100 * 1024;  // per CTA (two per SM)
 template <int K, int W, bool BWD>
 struct HwGeo {
   static constexpr int HPT = kVec / K;
-  static constexpr int TR = BWD ? 16 : (K == kVec ? 64 : 16);
+  static constexpr int TR = K == kVec ? (BWD ? 32 : 64) : 16;
   static constexpr int RPT = TR / kNC;
   static_assert(RPT * kNC == TR, "rows per tile must split over the compute warps");
   static constexpr int ROWS_X = TR + W - 1;           // x rows t0-(W-1) .. t0+TR-1
@@ -353,61 +353,111 @@ __global__ void __launch_bounds__(kHwThreads, kCtasPerSm)
       }
     } else {
       const __nv_bfloat16* dys = reinterpret_cast<const __nv_bfloat16*>(st + G::X_BYTES);
-      // dy rows r0 .. r0+RPT+W-2 (step t0 + i); x rows r0 .. r0+RPT+W-2 (step t0 - (W-1) + i)
-      float2 dyf[RPT + W - 1][P], xf[RPT + W - 1][P];
+      if constexpr (K == kVec) {
+        // One pass over the warp's input rows i = 0 .. RPT+W-2 (dy and weight row r0 + i,
+        // step t0 + r0 + i), every row loaded once:
+        //   dx[t] = sum_w (weight[t+w, h, w] + static_w[w]) * dy[t+w]  (+ dy[t]): input row
+        //       i adds its tap-w term to the pending dx row i - w (a ring of W rows, row rr
+        //       in slot rr % W); row i - (W-1) is then complete and stored;
+        //   P_w = dy[t] * x[t-w] for output row i (i < RPT): dstatic_w sums (per channel)
+        //       and dweight (summed over the head's channels), with x from a ring of the
+        //       last W x rows (x row r0 + k in slot k % W).
+        // Every sum sees its terms in the order of the per-row loop below (residual, then
+        // taps w = 0 .. W-1; rows in order), so both paths round alike.
+        float2 dxa[W][P], xw[W][P];
 #pragma unroll
-      for (int i = 0; i < RPT + W - 1; ++i) {
-        unpackv2(ld_lane<SPLIT>(dys + (r0 + i) * kCB, lane), dyf[i]);
-        unpackv2(ld_lane<SPLIT>(xs + (r0 + i) * kCB, lane), xf[i]);
-      }
-      // dx[t] = sum_w (weight[t+w, h, w] + static_w[w]) * dy[t+w]  (+ dy[t]).  Weight row
-      // j (step t0 + r0 + j) is read once and feeds dx rows j - w.
-      float2 dxv[RPT][P];
+        for (int k2 = 0; k2 < W - 1; ++k2) unpackv2(ld_lane<SPLIT>(xs + (r0 + k2) * kCB, lane), xw[k2 % W]);
 #pragma unroll
-      for (int rr = 0; rr < RPT; ++rr)
+        for (int i = 0; i < RPT + W - 1; ++i) {
+          float2 dyr[P];
+          unpackv2(ld_lane<SPLIT>(dys + (r0 + i) * kCB, lane), dyr);
+          float wt[HPT][W];
+          load_row_weights<K, W, SPLIT>(ws + (r0 + i) * wb, lane, log2hs, wt);
+          if (i < RPT) {
 #pragma unroll
-        for (int q = 0; q < P; ++q) dxv[rr][q] = residual ? dyf[rr][q] : make_float2(0.f, 0.f);
+            for (int q = 0; q < P; ++q) dxa[i % W][q] = residual ? dyr[q] : make_float2(0.f, 0.f);
+          }
 #pragma unroll
-      for (int j = 0; j < RPT + W - 1; ++j) {
-        float wt[HPT][W];
-        load_row_weights<K, W, SPLIT>(ws + (r0 + j) * wb, lane, log2hs, wt);
+          for (int w = 0; w < W; ++w) {
+            const int rr = i - w;
+            if (rr >= 0 && rr < RPT) {
 #pragma unroll
-        for (int w = 0; w < W; ++w) {
-          const int rr = j - w;
-          if (rr >= 0 && rr < RPT) {
+              for (int q = 0; q < P; ++q) {
+                const float2 coef = add2(make_float2(wt[0][w], wt[0][w]), s2[w][q]);
+                dxa[rr % W][q] = fma2(coef, dyr[q], dxa[rr % W][q]);
+              }
+            }
+          }
+          if (i >= W - 1 && i - (W - 1) < RPT) {
+            const int t = t0 + r0 + i - (W - 1);
+            if (dok && t < T) st_lane<SPLIT>(out + ((size_t)b * T + t) * D + d0, lane, packv2(dxa[(i - (W - 1)) % W]));
+          }
+          if (i < RPT) {
+            const int t = t0 + r0 + i;
+            const bool row_ok = dok && t < T;
+            // x row r0 + i + W - 1 (step t) joins the ring; x[t - w] is in slot (i + W - 1 - w) % W
+            unpackv2(ld_lane<SPLIT>(xs + (r0 + i + W - 1) * kCB, lane), xw[(i + W - 1) % W]);
 #pragma unroll
-            for (int q = 0; q < P; ++q) {
-              const float2 coef = add2(make_float2(wt[(2 * q) / K][w], wt[(2 * q + 1) / K][w]), s2[w][q]);
-              dxv[rr][q] = fma2(coef, dyf[j][q], dxv[rr][q]);
+            for (int w = 0; w < W; ++w)
+#pragma unroll
+              for (int q = 0; q < P; ++q) acc_sw[w][q] = fma2(dyr[q], xw[(i + W - 1 - w) % W][q], acc_sw[w][q]);
+            // one head per lane: sum the lane's channels, then over the hs/4 lanes of the head
+            float hsum[W];
+#pragma unroll
+            for (int w = 0; w < W; ++w) {
+              const float2(&xr)[P] = xw[(i + W - 1 - w) % W];
+              float2 a = mul2(dyr[0], xr[0]);
+#pragma unroll
+              for (int q = 1; q < P; ++q) a = fma2(dyr[q], xr[q], a);
+              hsum[w] = a.x + a.y;
+            }
+            head_reduce_store<W, LG>(hsum, lane, row_ok, dw + (((size_t)b * T + t) * H + (dch >> log2hs)) * W);
+          }
+        }
+      } else {
+        // head_size 1 or 2 (several heads per lane, 16-row tiles): every row of the warp's
+        // window in registers, then a per-row loop.
+        // dy rows r0 .. r0+RPT+W-2 (step t0 + i); x rows r0 .. r0+RPT+W-2 (step t0 - (W-1) + i)
+        float2 dyf[RPT + W - 1][P], xf[RPT + W - 1][P];
+#pragma unroll
+        for (int i = 0; i < RPT + W - 1; ++i) {
+          unpackv2(ld_lane<SPLIT>(dys + (r0 + i) * kCB, lane), dyf[i]);
+          unpackv2(ld_lane<SPLIT>(xs + (r0 + i) * kCB, lane), xf[i]);
+        }
+        // dx[t] = sum_w (weight[t+w, h, w] + static_w[w]) * dy[t+w]  (+ dy[t]).  Weight row
+        // j (step t0 + r0 + j) is read once and feeds dx rows j - w.
+        float2 dxv[RPT][P];
+#pragma unroll
+        for (int rr = 0; rr < RPT; ++rr)
+#pragma unroll
+          for (int q = 0; q < P; ++q) dxv[rr][q] = residual ? dyf[rr][q] : make_float2(0.f, 0.f);
+#pragma unroll
+        for (int j = 0; j < RPT + W - 1; ++j) {
+          float wt[HPT][W];
+          load_row_weights<K, W, SPLIT>(ws + (r0 + j) * wb, lane, log2hs, wt);
+#pragma unroll
+          for (int w = 0; w < W; ++w) {
+            const int rr = j - w;
+            if (rr >= 0 && rr < RPT) {
+#pragma unroll
+              for (int q = 0; q < P; ++q) {
+                const float2 coef = add2(make_float2(wt[(2 * q) / K][w], wt[(2 * q + 1) / K][w]), s2[w][q]);
+                dxv[rr][q] = fma2(coef, dyf[j][q], dxv[rr][q]);
+              }
             }
           }
         }
-      }
 #pragma unroll
-      for (int rr = 0; rr < RPT; ++rr) {
-        const int t = t0 + r0 + rr;
-        const bool row_ok = dok && t < T;
-        if (row_ok) st_lane<SPLIT>(out + ((size_t)b * T + t) * D + d0, lane, packv2(dxv[rr]));
-        // P_w = dy[t] * x[t-w]: dstatic_w (per channel, fused multiply-add) and
-        // dweight (summed over the head's channels)
+        for (int rr = 0; rr < RPT; ++rr) {
+          const int t = t0 + r0 + rr;
+          const bool row_ok = dok && t < T;
+          if (row_ok) st_lane<SPLIT>(out + ((size_t)b * T + t) * D + d0, lane, packv2(dxv[rr]));
+          // P_w = dy[t] * x[t-w]: dstatic_w (per channel, fused multiply-add) and
+          // dweight (HPT heads per lane, K channels each)
 #pragma unroll
-        for (int w = 0; w < W; ++w)
+          for (int w = 0; w < W; ++w)
 #pragma unroll
-          for (int q = 0; q < P; ++q) acc_sw[w][q] = fma2(dyf[rr][q], xf[rr + W - 1 - w][q], acc_sw[w][q]);
-        if constexpr (K == kVec) {
-          // one head per lane: sum the lane's channels, then over the hs/4 lanes of the head
-          float hsum[W];
-#pragma unroll
-          for (int w = 0; w < W; ++w) {
-            float2 a = mul2(dyf[rr][0], xf[rr + W - 1 - w][0]);
-#pragma unroll
-            for (int q = 1; q < P; ++q) a = fma2(dyf[rr][q], xf[rr + W - 1 - w][q], a);
-            hsum[w] = a.x + a.y;
-          }
-          head_reduce_store<W, LG>(hsum, lane, row_ok,
-                               dw + (((size_t)b * T + t) * H + (dch >> log2hs)) * W);
-        } else {
-          // HPT heads per lane, K channels each (K = 1 or 2)
+            for (int q = 0; q < P; ++q) acc_sw[w][q] = fma2(dyf[rr][q], xf[rr + W - 1 - w][q], acc_sw[w][q]);
           __align__(16) __nv_bfloat16 v[HPT * W];
 #pragma unroll
           for (int w = 0; w < W; ++w)
@@ -482,7 +532,7 @@ HwSplit hw_split(int64_t B, int64_t T, int64_t D, int TR) {
   return sp;
 }
 
-int hw_tr(int K, bool bwd) { return bwd ? 16 : (K == kVec ? 64 : 16); }
+int hw_tr(int K, bool bwd) { return K == kVec ? (bwd ? 32 : 64) : 16; }
 
 template <int K, int W, bool BWD, bool SPLIT, int LG>
 int launch_hw_tma(const void* x, const void* wgt, const void* sw, const void* dy, void* out, void* dw, float* part,
