@@ -30,161 +30,366 @@ __device__ __forceinline__ float uext(const T* __restrict__ U, const T* __restri
   return r < R ? Elem<T>::to_f(U[((size_t)r * W + w) * D + d]) : Elem<T>::to_f(sw[(size_t)w * D + d]);
 }
 
+constexpr int kMaxRk = 64;  // R_kernel bound of these kernels (dz keeps 8 ranks per warp x 8 warps)
+
 }  // namespace
 
-// y[b,t,d]; one thread per (token, channel)
+// The bf16 path rounds the products dy * x_shift to bf16 before the dz / dU sums, as
+// the reference's bf16 kernel does (lowrank.py:127-129); the float32 path keeps them.
 template <typename T>
-__global__ void __launch_bounds__(256) lr_fwd_simple_kernel(const T* __restrict__ x, const T* __restrict__ z,
-                                                            const T* __restrict__ U, const T* __restrict__ sw,
-                                                            T* __restrict__ y, int Tlen, int D, int R, int Rk, int W,
-                                                            int residual) {
-  const int d = blockIdx.y * blockDim.x + threadIdx.x;
-  const int64_t tok = blockIdx.x;  // b*T + t
-  if (d >= D) return;
-  const int t = (int)(tok % Tlen);
-  const T* zrow = z + tok * R;
-  float acc = 0.f;
-  for (int w = 0; w < W; ++w) {
-    if (t - w < 0) break;
-    float k = 0.f;
-    for (int r = 0; r < Rk; ++r) k = fmaf(zext(zrow, r, R), uext(U, sw, r, w, d, R, D, W), k);
-    acc = fmaf(k, Elem<T>::to_f(x[(tok - w) * D + d]), acc);
-  }
-  if (residual) acc += Elem<T>::to_f(x[tok * D + d]);
-  y[tok * D + d] = Elem<T>::from_f(acc);
+__device__ __forceinline__ float round_p(float v) {
+  if constexpr (sizeof(T) == 2) return __bfloat162float(__float2bfloat16_rn(v));
+  else return v;
 }
 
-// dx[b,t,d] = sum_w dy[t+w,d] * K[t+w,w,d]  (+ dy[t,d])
-template <typename T>
-__global__ void __launch_bounds__(256) lr_dx_simple_kernel(const T* __restrict__ z, const T* __restrict__ U,
-                                                           const T* __restrict__ sw, const T* __restrict__ dy,
-                                                           T* __restrict__ dx, int Tlen, int D, int R, int Rk, int W,
-                                                           int residual) {
-  const int d = blockIdx.y * blockDim.x + threadIdx.x;
-  const int64_t tok = blockIdx.x;
-  if (d >= D) return;
-  const int t = (int)(tok % Tlen);
-  float acc = 0.f;
-  for (int w = 0; w < W; ++w) {
-    if (t + w >= Tlen) break;
-    const T* zrow = z + (tok + w) * R;
-    float k = 0.f;
-    for (int r = 0; r < Rk; ++r) k = fmaf(zext(zrow, r, R), uext(U, sw, r, w, d, R, D, W), k);
-    acc = fmaf(k, Elem<T>::to_f(dy[(tok + w) * D + d]), acc);
-  }
-  if (residual) acc += Elem<T>::to_f(dy[tok * D + d]);
-  dx[tok * D + d] = Elem<T>::from_f(acc);
-}
+// ---------------------------------------------------------------------------- y and dx
+// y[tok, d]  = sum_w K_w(tok) x[tok - w, d] (+ x[tok, d])           (DX = false)
+// dx[tok, d] = sum_w K_w(tok + w) dy[tok + w, d] (+ dy[tok, d])      (DX = true)
+// with K_w(s)[d] = sum_r z_ext[s, r] U_ext[r, w, d] (lowrank.py:24-67, 158-205).  A block
+// owns 64 channels x 64 tokens: the U_ext block [Rk][W][64] and the tile's z_ext rows are
+// staged in shared memory once (fp32), so U is read once per tile instead of once per
+// token.  Thread (channel c, token subgroup) computes 4 consecutive tokens at a time: per
+// rank it loads the W values U[r][.][c] and the z values of its tokens once and does
+// 4 x W multiply-adds with them.
+constexpr int kKxCh = 64, kKxTok = 64, kKxGrp = 4;
 
-// dz[b,t,r] = sum_{w,d} dy[t,d] x[t-w,d] U[r,w,d], r < R; one block (256 threads) per token.
-constexpr int kMaxRk = 64;
-template <typename T>
-__global__ void __launch_bounds__(256) lr_dz_simple_kernel(const T* __restrict__ x, const T* __restrict__ U,
-                                                           const T* __restrict__ dy, T* __restrict__ dz, int Tlen,
-                                                           int D, int R, int W) {
-  const int64_t tok = blockIdx.x;
-  const int t = (int)(tok % Tlen);
-  float acc[kMaxRk];
-#pragma unroll
-  for (int r = 0; r < kMaxRk; ++r) acc[r] = 0.f;
-  for (int d = threadIdx.x; d < D; d += blockDim.x) {
-    const float g = Elem<T>::to_f(dy[tok * D + d]);
-    for (int w = 0; w < W && t - w >= 0; ++w) {
-      const float p = g * Elem<T>::to_f(x[(tok - w) * D + d]);
-#pragma unroll
-      for (int r = 0; r < kMaxRk; ++r)
-        if (r < R) acc[r] = fmaf(p, Elem<T>::to_f(U[((size_t)r * W + w) * D + d]), acc[r]);
-    }
+template <typename T, bool DX, int W>
+__global__ void __launch_bounds__(256) lr_kx_tiled_kernel(const T* __restrict__ xin, const T* __restrict__ z,
+                                                          const T* __restrict__ U, const T* __restrict__ sw,
+                                                          T* __restrict__ out, int64_t ntok, int Tlen, int D, int R,
+                                                          int Rk, int residual) {
+  extern __shared__ float smf[];
+  float* us = smf;                       // [Rk][W][kKxCh]
+  float* zs = us + Rk * W * kKxCh;       // [kKxTok + W - 1][Rk]
+  const int d0 = blockIdx.x * kKxCh;
+  const int64_t k0 = (int64_t)blockIdx.y * kKxTok;
+  for (int i = threadIdx.x; i < Rk * W * kKxCh; i += blockDim.x) {
+    const int cc = i % kKxCh, rw = i / kKxCh, w = rw % W, r = rw / W, d = d0 + cc;
+    us[i] = d < D ? uext(U, sw, r, w, d, R, D, W) : 0.f;
   }
-  __shared__ float red[8][kMaxRk];
-  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-#pragma unroll
-  for (int r = 0; r < kMaxRk; ++r) {
-    if (r < R) {
-      float v = acc[r];
-#pragma unroll
-      for (int off = 16; off > 0; off >>= 1) v += __shfl_xor_sync(0xffffffffu, v, off);
-      if (lane == 0) red[warp][r] = v;
-    }
+  const int nz = kKxTok + (DX ? W - 1 : 0);
+  for (int i = threadIdx.x; i < nz * Rk; i += blockDim.x) {
+    const int row = i / Rk, r = i % Rk;
+    const int64_t k = k0 + row;
+    zs[i] = k < ntok ? zext(z + k * R, r, R) : 0.f;
   }
   __syncthreads();
-  if (threadIdx.x < R) {
-    float v = 0.f;
-    for (int wp = 0; wp < (int)(blockDim.x >> 5); ++wp) v += red[wp][threadIdx.x];
-    dz[tok * R + threadIdx.x] = Elem<T>::from_f(v);
-  }
-}
-
-// part[chunk][r][w*D + d] = sum_{tok in chunk} z_ext[tok,r] dy[tok,d] x[tok-w,d]
-// grid: (ceil(D/256), Rk*W, nchunks)
-template <typename T>
-__global__ void __launch_bounds__(256) lr_du_simple_kernel(const T* __restrict__ x, const T* __restrict__ z,
-                                                           const T* __restrict__ dy, float* __restrict__ part,
-                                                           int64_t ntok, int Tlen, int D, int R, int Rk, int W,
-                                                           int chunk) {
-  const int d = blockIdx.x * blockDim.x + threadIdx.x;
-  const int r = blockIdx.y / W, w = blockIdx.y % W;
-  const int64_t c = blockIdx.z;
+  const int c = threadIdx.x % kKxCh, sub = threadIdx.x / kKxCh;
+  const int d = d0 + c;
   if (d >= D) return;
-  const int64_t tbeg = c * chunk;
-  const int64_t tend = min(tbeg + (int64_t)chunk, ntok);
-  float acc = 0.f;
-  for (int64_t tok = tbeg; tok < tend; ++tok) {
-    const int t = (int)(tok % Tlen);
-    if (t - w < 0) continue;
-    const float zz = r < R ? Elem<T>::to_f(z[tok * R + r]) : 1.f;
-    acc = fmaf(zz * Elem<T>::to_f(dy[tok * D + d]), Elem<T>::to_f(x[(tok - w) * D + d]), acc);
+  constexpr int NZ = DX ? kKxGrp + W - 1 : kKxGrp;  // z rows a group of tokens reads
+  for (int j0 = sub * kKxGrp; j0 < kKxTok; j0 += (256 / kKxCh) * kKxGrp) {
+    if (k0 + j0 >= ntok) break;
+    // K[tt][w] = K_w(token j0 + tt (+ w for dx)), summed over r in order
+    float K[kKxGrp][W];
+#pragma unroll
+    for (int tt = 0; tt < kKxGrp; ++tt)
+#pragma unroll
+      for (int w = 0; w < W; ++w) K[tt][w] = 0.f;
+    for (int r = 0; r < Rk; ++r) {
+      float u[W], zr[NZ];
+#pragma unroll
+      for (int w = 0; w < W; ++w) u[w] = us[(r * W + w) * kKxCh + c];
+#pragma unroll
+      for (int i = 0; i < NZ; ++i) zr[i] = zs[(j0 + i) * Rk + r];
+#pragma unroll
+      for (int tt = 0; tt < kKxGrp; ++tt)
+#pragma unroll
+        for (int w = 0; w < W; ++w) K[tt][w] = fmaf(zr[DX ? tt + w : tt], u[w], K[tt][w]);
+    }
+    int t = (int)((k0 + j0) % Tlen);  // position of the group's first token in its sequence
+#pragma unroll
+    for (int tt = 0; tt < kKxGrp; ++tt, t = (t + 1 == Tlen) ? 0 : t + 1) {
+      const int64_t tok = k0 + j0 + tt;
+      if (tok < ntok) {
+        float acc = 0.f;
+#pragma unroll
+        for (int w = 0; w < W; ++w) {
+          if (DX ? (t + w >= Tlen) : (t - w < 0)) break;
+          acc = fmaf(K[tt][w], Elem<T>::to_f(xin[(DX ? tok + w : tok - w) * D + d]), acc);
+        }
+        if (residual) acc += Elem<T>::to_f(xin[tok * D + d]);
+        out[tok * D + d] = Elem<T>::from_f(acc);
+      }
+    }
   }
-  part[(c * Rk + r) * (int64_t)W * D + (int64_t)w * D + d] = acc;
 }
 
-namespace {
+// ---------------------------------------------------------------------------- dz
+// dz[tok, r] = sum_{w,d} P_w[tok, d] U[r, w, d],  P_w = dy[tok, d] x[tok - w, d], r < R
+// (lowrank.py:86-140).  A block owns 32 tokens and walks D in 32-channel chunks: dy, x
+// (with the W-1 rows before the tile) and the U chunk [R][W][32] are staged in shared
+// memory, the products P once per chunk, then thread (token = lane, rank group = warp)
+// accumulates ranks 8 warp .. 8 warp + 7 over the chunk, reading them as two float4s from
+// the U chunk stored [W][channel][rank] (a broadcast within the warp).  U is read once per
+// 32 tokens.
+constexpr int kDzTok = 32, kDzCh = 32, kDzPad = kDzCh + 1;
+
+template <typename T, int W>
+__global__ void __launch_bounds__(256) lr_dz_tiled_kernel(const T* __restrict__ x, const T* __restrict__ U,
+                                                          const T* __restrict__ dy, T* __restrict__ dz, int64_t ntok,
+                                                          int Tlen, int D, int R) {
+  extern __shared__ float smf[];
+  const int RP = (R + 7) / 8 * 8 + 4;             // a channel's ranks: whole float4 pairs, + 4 against bank conflicts
+  float* us = smf;                                // [W][kDzCh][RP]
+  float* ps = us + W * kDzCh * RP;                // [W][kDzTok][kDzPad]
+  float* dys = ps + W * kDzTok * kDzPad;          // [kDzTok][kDzPad]
+  float* xs = dys + kDzTok * kDzPad;              // [kDzTok + W - 1][kDzPad]
+  __shared__ int tpos[kDzTok];                    // position of each token in its sequence
+  const int64_t k0 = (int64_t)blockIdx.x * kDzTok;
+  const int lane = threadIdx.x & 31, rg = threadIdx.x >> 5;
+  if (threadIdx.x < kDzTok) tpos[threadIdx.x] = (int)((k0 + threadIdx.x) % Tlen);
+  float acc[8];
+#pragma unroll
+  for (int i = 0; i < 8; ++i) acc[i] = 0.f;
+  for (int dc0 = 0; dc0 < D; dc0 += kDzCh) {
+    __syncthreads();  // the previous chunk's reads are done
+    for (int i = threadIdx.x; i < kDzTok * kDzCh; i += blockDim.x) {
+      const int row = i / kDzCh, cc = i % kDzCh, d = dc0 + cc;
+      const int64_t k = k0 + row;
+      dys[row * kDzPad + cc] = (k < ntok && d < D) ? Elem<T>::to_f(dy[k * D + d]) : 0.f;
+    }
+    for (int i = threadIdx.x; i < (kDzTok + W - 1) * kDzCh; i += blockDim.x) {
+      const int row = i / kDzCh, cc = i % kDzCh, d = dc0 + cc;
+      const int64_t k = k0 - (W - 1) + row;
+      xs[row * kDzPad + cc] = (k >= 0 && k < ntok && d < D) ? Elem<T>::to_f(x[k * D + d]) : 0.f;
+    }
+    const int RQ = (R + 7) / 8 * 8;
+    for (int i = threadIdx.x; i < RQ * W * kDzCh; i += blockDim.x) {
+      const int cc = i % kDzCh, rw = i / kDzCh, w = rw % W, r = rw / W, d = dc0 + cc;
+      us[(w * kDzCh + cc) * RP + r] = (d < D && r < R) ? Elem<T>::to_f(U[((size_t)r * W + w) * D + d]) : 0.f;
+    }
+    __syncthreads();
+    for (int i = threadIdx.x; i < W * kDzTok * kDzCh; i += blockDim.x) {
+      const int cc = i % kDzCh, j = (i / kDzCh) % kDzTok, w = i / (kDzCh * kDzTok);
+      const int64_t tok = k0 + j;
+      float p = 0.f;
+      if (tok < ntok && tpos[j] - w >= 0)
+        p = round_p<T>(dys[j * kDzPad + cc] * xs[(j + W - 1 - w) * kDzPad + cc]);
+      ps[(w * kDzTok + j) * kDzPad + cc] = p;
+    }
+    __syncthreads();
+    if (8 * rg < R) {
+      for (int w = 0; w < W; ++w) {
+        const float* pr = ps + (w * kDzTok + lane) * kDzPad;
+        const float* ur = us + (w * kDzCh) * RP + 8 * rg;
+#pragma unroll 4
+        for (int cc = 0; cc < kDzCh; ++cc) {
+          const float p = pr[cc];
+          const float4 u0 = *reinterpret_cast<const float4*>(ur + cc * RP);
+          const float4 u1 = *reinterpret_cast<const float4*>(ur + cc * RP + 4);
+          acc[0] = fmaf(p, u0.x, acc[0]);
+          acc[1] = fmaf(p, u0.y, acc[1]);
+          acc[2] = fmaf(p, u0.z, acc[2]);
+          acc[3] = fmaf(p, u0.w, acc[3]);
+          acc[4] = fmaf(p, u1.x, acc[4]);
+          acc[5] = fmaf(p, u1.y, acc[5]);
+          acc[6] = fmaf(p, u1.z, acc[6]);
+          acc[7] = fmaf(p, u1.w, acc[7]);
+        }
+      }
+    }
+  }
+  const int64_t tok = k0 + lane;
+  if (tok < ntok) {
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      const int r = 8 * rg + i;
+      if (r < R) dz[tok * R + r] = Elem<T>::from_f(acc[i]);
+    }
+  }
+}
+
+// ---------------------------------------------------------------------------- dU
+// part[chunk][r][w*D + d] = sum_{tok in chunk} z_ext[tok, r] P_w[tok, d]  (lowrank.py:126-137,
+// without the atomics).  Thread = channel; block (channel block, 8 ranks, token chunk).  The
+// thread walks its chunk once, keeping the last W x values in registers, and accumulates
+// [8 ranks][W taps]; dy and x are read once per group of 8 ranks.
 constexpr int kDuChunk = 256;
+
+template <typename T, int W>
+__global__ void __launch_bounds__(128) lr_du_tiled_kernel(const T* __restrict__ x, const T* __restrict__ z,
+                                                          const T* __restrict__ dy, float* __restrict__ part,
+                                                          int64_t ntok, int Tlen, int D, int R, int Rk) {
+  __shared__ float zsh[kDuChunk][8];  // z_ext of the chunk's tokens, this block's 8 ranks
+  const int d = blockIdx.x * blockDim.x + threadIdx.x;
+  const int r0 = blockIdx.y * 8;
+  const int64_t c = blockIdx.z;
+  const int64_t tbeg = c * kDuChunk;
+  const int64_t tend = min(tbeg + (int64_t)kDuChunk, ntok);
+  for (int i = threadIdx.x; i < kDuChunk * 8; i += blockDim.x) {
+    const int j = i / 8, r = r0 + i % 8;
+    const int64_t tok = tbeg + j;
+    zsh[j][i % 8] = (tok < tend && r < Rk) ? (r < R ? Elem<T>::to_f(z[tok * R + r]) : 1.f) : 0.f;
+  }
+  __syncthreads();
+  if (d >= D) return;
+  float acc[8][W];
+#pragma unroll
+  for (int i = 0; i < 8; ++i)
+#pragma unroll
+    for (int w = 0; w < W; ++w) acc[i][w] = 0.f;
+  // xw[w] = x[tok - w, d] once token tok is loaded; before the first token it holds the
+  // chunk's look-behind x[tbeg - 1 - w] (values from another batch row are masked below)
+  float xw[W];
+#pragma unroll
+  for (int w = 0; w < W; ++w) xw[w] = tbeg - 1 - w >= 0 ? Elem<T>::to_f(x[(tbeg - 1 - w) * D + d]) : 0.f;
+  int t = (int)(tbeg % Tlen);
+#pragma unroll 4
+  for (int64_t tok = tbeg; tok < tend; ++tok) {
+#pragma unroll
+    for (int w = W - 1; w > 0; --w) xw[w] = xw[w - 1];
+    xw[0] = Elem<T>::to_f(x[tok * D + d]);
+    const float g = Elem<T>::to_f(dy[tok * D + d]);
+    float p[W];
+#pragma unroll
+    for (int w = 0; w < W; ++w) p[w] = t - w >= 0 ? round_p<T>(g * xw[w]) : 0.f;
+    const float* zr = zsh[tok - tbeg];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      const float zz = zr[i];  // 0 for ranks >= R_kernel (never stored)
+#pragma unroll
+      for (int w = 0; w < W; ++w) acc[i][w] = fmaf(zz, p[w], acc[i][w]);
+    }
+    if (++t == Tlen) t = 0;
+  }
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    const int r = r0 + i;
+    if (r < Rk) {
+#pragma unroll
+      for (int w = 0; w < W; ++w) part[(c * Rk + r) * (int64_t)W * D + (int64_t)w * D + d] = acc[i][w];
+    }
+  }
 }
 
 int64_t lr_simple_partial_rows(int64_t B, int64_t T) { return (B * T + kDuChunk - 1) / kDuChunk; }
 
+namespace {
+
+template <typename K>
+int set_smem(K kern, size_t bytes, const char* what) {
+  if (bytes <= 48 * 1024) return DYNCONV_OK;
+  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)bytes);
+  if (e != cudaSuccess) {
+    cudaGetLastError();
+    return cuda_status(e, what);
+  }
+  return DYNCONV_OK;
+}
+
+template <typename E, bool DX, int W>
+int launch_kx_w(const void* xin, const void* z, const void* U, const void* sw, void* out, int64_t B, int64_t Tlen,
+                int64_t D, int R, int Rk, int residual, cudaStream_t st) {
+  const int64_t ntok = B * Tlen;
+  const size_t smem = ((size_t)Rk * W * kKxCh + (size_t)(kKxTok + W - 1) * Rk) * sizeof(float);
+  auto kern = lr_kx_tiled_kernel<E, DX, W>;
+  if (int s = set_smem(kern, smem, "cudaFuncSetAttribute(lr_kx_tiled)")) return s;
+  dim3 grid((unsigned)((D + kKxCh - 1) / kKxCh), (unsigned)((ntok + kKxTok - 1) / kKxTok));
+  kern<<<grid, 256, smem, st>>>((const E*)xin, (const E*)z, (const E*)U, (const E*)sw, (E*)out, ntok, (int)Tlen, (int)D,
+                                R, Rk, residual);
+  DYNCONV_CHECK_LAUNCH(DX ? "lr_kx_tiled_kernel(dx)" : "lr_kx_tiled_kernel(y)");
+  return DYNCONV_OK;
+}
+
+template <typename E, bool DX>
+int launch_kx(const void* xin, const void* z, const void* U, const void* sw, void* out, int64_t B, int64_t Tlen,
+              int64_t D, int R, int Rk, int W, int residual, cudaStream_t st) {
+  switch (W) {
+    case 1: return launch_kx_w<E, DX, 1>(xin, z, U, sw, out, B, Tlen, D, R, Rk, residual, st);
+    case 2: return launch_kx_w<E, DX, 2>(xin, z, U, sw, out, B, Tlen, D, R, Rk, residual, st);
+    case 3: return launch_kx_w<E, DX, 3>(xin, z, U, sw, out, B, Tlen, D, R, Rk, residual, st);
+    case 4: return launch_kx_w<E, DX, 4>(xin, z, U, sw, out, B, Tlen, D, R, Rk, residual, st);
+    case 5: return launch_kx_w<E, DX, 5>(xin, z, U, sw, out, B, Tlen, D, R, Rk, residual, st);
+    case 6: return launch_kx_w<E, DX, 6>(xin, z, U, sw, out, B, Tlen, D, R, Rk, residual, st);
+    case 7: return launch_kx_w<E, DX, 7>(xin, z, U, sw, out, B, Tlen, D, R, Rk, residual, st);
+    case 8: return launch_kx_w<E, DX, 8>(xin, z, U, sw, out, B, Tlen, D, R, Rk, residual, st);
+    default: return set_error(DYNCONV_ERR_UNSUPPORTED, "W=%d not supported (1..8)", W);
+  }
+}
+
+template <typename E, int W>
+int launch_dz_w(const void* x, const void* U, const void* dy, void* dz, int64_t B, int64_t Tlen, int64_t D, int R,
+                cudaStream_t st) {
+  const int64_t ntok = B * Tlen;
+  const size_t smem = ((size_t)((R + 7) / 8 * 8 + 4) * W * kDzCh + (size_t)W * kDzTok * kDzPad +
+                       (size_t)kDzTok * kDzPad + (size_t)(kDzTok + W - 1) * kDzPad) * sizeof(float);
+  auto kern = lr_dz_tiled_kernel<E, W>;
+  if (int s = set_smem(kern, smem, "cudaFuncSetAttribute(lr_dz_tiled)")) return s;
+  kern<<<(unsigned)((ntok + kDzTok - 1) / kDzTok), 256, smem, st>>>((const E*)x, (const E*)U, (const E*)dy, (E*)dz,
+                                                                    ntok, (int)Tlen, (int)D, R);
+  DYNCONV_CHECK_LAUNCH("lr_dz_tiled_kernel");
+  return DYNCONV_OK;
+}
+
+template <typename E>
+int launch_dz(const void* x, const void* U, const void* dy, void* dz, int64_t B, int64_t Tlen, int64_t D, int R, int W,
+              cudaStream_t st) {
+  switch (W) {
+    case 1: return launch_dz_w<E, 1>(x, U, dy, dz, B, Tlen, D, R, st);
+    case 2: return launch_dz_w<E, 2>(x, U, dy, dz, B, Tlen, D, R, st);
+    case 3: return launch_dz_w<E, 3>(x, U, dy, dz, B, Tlen, D, R, st);
+    case 4: return launch_dz_w<E, 4>(x, U, dy, dz, B, Tlen, D, R, st);
+    case 5: return launch_dz_w<E, 5>(x, U, dy, dz, B, Tlen, D, R, st);
+    case 6: return launch_dz_w<E, 6>(x, U, dy, dz, B, Tlen, D, R, st);
+    case 7: return launch_dz_w<E, 7>(x, U, dy, dz, B, Tlen, D, R, st);
+    case 8: return launch_dz_w<E, 8>(x, U, dy, dz, B, Tlen, D, R, st);
+    default: return set_error(DYNCONV_ERR_UNSUPPORTED, "W=%d not supported (1..8)", W);
+  }
+}
+
+template <typename E, int W>
+int launch_du_w(const void* x, const void* z, const void* dy, float* part, int64_t B, int64_t Tlen, int64_t D, int R,
+                int Rk, cudaStream_t st) {
+  const int64_t ntok = B * Tlen;
+  dim3 grid((unsigned)((D + 127) / 128), (unsigned)((Rk + 7) / 8), (unsigned)lr_simple_partial_rows(B, Tlen));
+  lr_du_tiled_kernel<E, W><<<grid, 128, 0, st>>>((const E*)x, (const E*)z, (const E*)dy, part, ntok, (int)Tlen, (int)D, R,
+                                                 Rk);
+  DYNCONV_CHECK_LAUNCH("lr_du_tiled_kernel");
+  return DYNCONV_OK;
+}
+
+template <typename E>
+int launch_du(const void* x, const void* z, const void* dy, float* part, int64_t B, int64_t Tlen, int64_t D, int R,
+              int Rk, int W, cudaStream_t st) {
+  switch (W) {
+    case 1: return launch_du_w<E, 1>(x, z, dy, part, B, Tlen, D, R, Rk, st);
+    case 2: return launch_du_w<E, 2>(x, z, dy, part, B, Tlen, D, R, Rk, st);
+    case 3: return launch_du_w<E, 3>(x, z, dy, part, B, Tlen, D, R, Rk, st);
+    case 4: return launch_du_w<E, 4>(x, z, dy, part, B, Tlen, D, R, Rk, st);
+    case 5: return launch_du_w<E, 5>(x, z, dy, part, B, Tlen, D, R, Rk, st);
+    case 6: return launch_du_w<E, 6>(x, z, dy, part, B, Tlen, D, R, Rk, st);
+    case 7: return launch_du_w<E, 7>(x, z, dy, part, B, Tlen, D, R, Rk, st);
+    case 8: return launch_du_w<E, 8>(x, z, dy, part, B, Tlen, D, R, Rk, st);
+    default: return set_error(DYNCONV_ERR_UNSUPPORTED, "W=%d not supported (1..8)", W);
+  }
+}
+
+}  // namespace
+
 int lr_fwd_simple_launch(const void* x, const void* z, const void* U, const void* sw, void* y, int64_t B, int64_t T,
                          int64_t D, int R, int Rk, int W, int dtype, int residual, cudaStream_t st) {
-  dim3 grid((unsigned)(B * T), (unsigned)((D + 255) / 256));
+  if (Rk > kMaxRk) return set_error(DYNCONV_ERR_UNSUPPORTED, "R_kernel=%d > %d", Rk, kMaxRk);
   if (dtype == DYNCONV_DTYPE_BF16)
-    lr_fwd_simple_kernel<__nv_bfloat16><<<grid, 256, 0, st>>>(
-        (const __nv_bfloat16*)x, (const __nv_bfloat16*)z, (const __nv_bfloat16*)U, (const __nv_bfloat16*)sw,
-        (__nv_bfloat16*)y, (int)T, (int)D, R, Rk, W, residual);
-  else
-    lr_fwd_simple_kernel<float><<<grid, 256, 0, st>>>((const float*)x, (const float*)z, (const float*)U,
-                                                      (const float*)sw, (float*)y, (int)T, (int)D, R, Rk, W, residual);
-  DYNCONV_CHECK_LAUNCH("lr_fwd_simple_kernel");
-  return DYNCONV_OK;
+    return launch_kx<__nv_bfloat16, false>(x, z, U, sw, y, B, T, D, R, Rk, W, residual, st);
+  return launch_kx<float, false>(x, z, U, sw, y, B, T, D, R, Rk, W, residual, st);
 }
 
 // dx, dz, and the fp32 dU partial rows (to be summed by reduce_partials_launch).
 int lr_bwd_simple_launch(const void* x, const void* z, const void* U, const void* sw, const void* dy, void* dx,
                          void* dz, float* part, int64_t B, int64_t T, int64_t D, int R, int Rk, int W, int dtype,
                          int residual, cudaStream_t st) {
-  if (R > kMaxRk) return set_error(DYNCONV_ERR_UNSUPPORTED, "R=%d > %d", R, kMaxRk);
-  const int64_t ntok = B * T;
-  dim3 gdx((unsigned)ntok, (unsigned)((D + 255) / 256));
-  dim3 gdu((unsigned)((D + 255) / 256), (unsigned)(Rk * W), (unsigned)lr_simple_partial_rows(B, T));
+  if (Rk > kMaxRk) return set_error(DYNCONV_ERR_UNSUPPORTED, "R_kernel=%d > %d", Rk, kMaxRk);
+  int s;
   if (dtype == DYNCONV_DTYPE_BF16) {
     using T16 = __nv_bfloat16;
-    lr_dx_simple_kernel<T16><<<gdx, 256, 0, st>>>((const T16*)z, (const T16*)U, (const T16*)sw, (const T16*)dy,
-                                                  (T16*)dx, (int)T, (int)D, R, Rk, W, residual);
-    lr_dz_simple_kernel<T16><<<(unsigned)ntok, 256, 0, st>>>((const T16*)x, (const T16*)U, (const T16*)dy, (T16*)dz,
-                                                            (int)T, (int)D, R, W);
-    lr_du_simple_kernel<T16><<<gdu, 256, 0, st>>>((const T16*)x, (const T16*)z, (const T16*)dy, part, ntok, (int)T,
-                                                  (int)D, R, Rk, W, kDuChunk);
-  } else {
-    lr_dx_simple_kernel<float><<<gdx, 256, 0, st>>>((const float*)z, (const float*)U, (const float*)sw,
-                                                    (const float*)dy, (float*)dx, (int)T, (int)D, R, Rk, W, residual);
-    lr_dz_simple_kernel<float><<<(unsigned)ntok, 256, 0, st>>>((const float*)x, (const float*)U, (const float*)dy,
-                                                              (float*)dz, (int)T, (int)D, R, W);
-    lr_du_simple_kernel<float><<<gdu, 256, 0, st>>>((const float*)x, (const float*)z, (const float*)dy, part, ntok,
-                                                    (int)T, (int)D, R, Rk, W, kDuChunk);
+    if ((s = launch_kx<T16, true>(dy, z, U, sw, dx, B, T, D, R, Rk, W, residual, st))) return s;
+    if ((s = launch_dz<T16>(x, U, dy, dz, B, T, D, R, W, st))) return s;
+    return launch_du<T16>(x, z, dy, part, B, T, D, R, Rk, W, st);
   }
-  DYNCONV_CHECK_LAUNCH("lr_bwd_simple kernels");
-  note_launch(2);  // three kernels above, one counted by the check
-  return DYNCONV_OK;
+  if ((s = launch_kx<float, true>(dy, z, U, sw, dx, B, T, D, R, Rk, W, residual, st))) return s;
+  if ((s = launch_dz<float>(x, U, dy, dz, B, T, D, R, W, st))) return s;
+  return launch_du<float>(x, z, dy, part, B, T, D, R, Rk, W, st);
 }
 
 }  // namespace dynconv
