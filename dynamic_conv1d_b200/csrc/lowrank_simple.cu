@@ -119,10 +119,11 @@ __global__ void __launch_bounds__(256) lr_kx_tiled_kernel(const T* __restrict__ 
 // dz[tok, r] = sum_{w,d} P_w[tok, d] U[r, w, d],  P_w = dy[tok, d] x[tok - w, d], r < R
 // (lowrank.py:86-140).  A block owns 32 tokens and walks D in 32-channel chunks: dy, x
 // (with the W-1 rows before the tile) and the U chunk [R][W][32] are staged in shared
-// memory, the products P once per chunk, then thread (token = lane, rank group = warp)
-// accumulates ranks 8 warp .. 8 warp + 7 over the chunk, reading them as two float4s from
-// the U chunk stored [W][channel][rank] (a broadcast within the warp).  U is read once per
-// 32 tokens.
+// memory, the products P once per chunk.  Warp (rank group g, channel slice sl) accumulates
+// ranks 8g .. 8g + 7 of the 32 tokens (lane = token) over its slice of the chunk's channels,
+// reading the ranks as two float4s from the U chunk stored [W][channel][rank] (a broadcast
+// within the warp); with R <= 32 the 8 warps split the channels instead of idling.  The
+// slices' sums are added in slice order at the end.  U is read once per 32 tokens.
 constexpr int kDzTok = 32, kDzCh = 32, kDzPad = kDzCh + 1;
 
 template <typename T, int W>
@@ -135,9 +136,14 @@ __global__ void __launch_bounds__(256) lr_dz_tiled_kernel(const T* __restrict__ 
   float* ps = us + W * kDzCh * RP;                // [W][kDzTok][kDzPad]
   float* dys = ps + W * kDzTok * kDzPad;          // [kDzTok][kDzPad]
   float* xs = dys + kDzTok * kDzPad;              // [kDzTok + W - 1][kDzPad]
+  float* red = xs + (kDzTok + W - 1) * kDzPad;    // [8 warps][kDzTok][8 ranks]
   __shared__ int tpos[kDzTok];                    // position of each token in its sequence
   const int64_t k0 = (int64_t)blockIdx.x * kDzTok;
-  const int lane = threadIdx.x & 31, rg = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int NG = R <= 8 ? 1 : R <= 16 ? 2 : R <= 32 ? 4 : 8;  // rank groups (of 8)
+  const int NS = 8 / NG;                                       // channel slices per group
+  const int rg = warp % NG, sl = warp / NG;
+  const int cc_lo = sl * (kDzCh / NS), cc_hi = cc_lo + kDzCh / NS;
   if (threadIdx.x < kDzTok) tpos[threadIdx.x] = (int)((k0 + threadIdx.x) % Tlen);
   float acc[8];
 #pragma unroll
@@ -174,7 +180,7 @@ __global__ void __launch_bounds__(256) lr_dz_tiled_kernel(const T* __restrict__ 
         const float* pr = ps + (w * kDzTok + lane) * kDzPad;
         const float* ur = us + (w * kDzCh) * RP + 8 * rg;
 #pragma unroll 4
-        for (int cc = 0; cc < kDzCh; ++cc) {
+        for (int cc = cc_lo; cc < cc_hi; ++cc) {
           const float p = pr[cc];
           const float4 u0 = *reinterpret_cast<const float4*>(ur + cc * RP);
           const float4 u1 = *reinterpret_cast<const float4*>(ur + cc * RP + 4);
@@ -190,12 +196,19 @@ __global__ void __launch_bounds__(256) lr_dz_tiled_kernel(const T* __restrict__ 
       }
     }
   }
+#pragma unroll
+  for (int i = 0; i < 8; ++i) red[(warp * kDzTok + lane) * 8 + i] = acc[i];
+  __syncthreads();
   const int64_t tok = k0 + lane;
-  if (tok < ntok) {
+  if (sl == 0 && tok < ntok) {
 #pragma unroll
     for (int i = 0; i < 8; ++i) {
       const int r = 8 * rg + i;
-      if (r < R) dz[tok * R + r] = Elem<T>::from_f(acc[i]);
+      if (r < R) {
+        float v = 0.f;
+        for (int s2 = 0; s2 < NS; ++s2) v += red[((rg + NG * s2) * kDzTok + lane) * 8 + i];
+        dz[tok * R + r] = Elem<T>::from_f(v);
+      }
     }
   }
 }
@@ -313,7 +326,8 @@ int launch_dz_w(const void* x, const void* U, const void* dy, void* dz, int64_t 
                 cudaStream_t st) {
   const int64_t ntok = B * Tlen;
   const size_t smem = ((size_t)((R + 7) / 8 * 8 + 4) * W * kDzCh + (size_t)W * kDzTok * kDzPad +
-                       (size_t)kDzTok * kDzPad + (size_t)(kDzTok + W - 1) * kDzPad) * sizeof(float);
+                       (size_t)kDzTok * kDzPad + (size_t)(kDzTok + W - 1) * kDzPad + (size_t)8 * kDzTok * 8) *
+                      sizeof(float);
   auto kern = lr_dz_tiled_kernel<E, W>;
   if (int s = set_smem(kern, smem, "cudaFuncSetAttribute(lr_dz_tiled)")) return s;
   kern<<<(unsigned)((ntok + kDzTok - 1) / kDzTok), 256, smem, st>>>((const E*)x, (const E*)U, (const E*)dy, (E*)dz,
