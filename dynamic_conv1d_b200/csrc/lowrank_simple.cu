@@ -1,5 +1,6 @@
 // lowrank_simple.cu -- CUDA-core lowrank kernels for the float32 path and for
-// shapes outside the tensor-core kernels' envelope (W > 4, R_kernel > 64 or odd D).
+// shapes outside the tensor-core kernels' envelope (W > 4; R_kernel > 32 in the
+// backward, > 64 in the forward; D not a multiple of 8; unaligned tensors).
 //
 // Reference behaviour: lowrank.py:24-67 (forward), lowrank.py:86-140 (dU/dz),
 // lowrank.py:158-205 (dx); oracle reference.py:23-39.  The reference's float32
@@ -8,9 +9,10 @@
 //
 // The static filter is folded in as rank R (z_ext[..., R] = 1, U_ext[R] = static_w)
 // by index arithmetic, never materialised in HBM (the reference pads/cats,
-// lowrank.py:222-226).  All reductions have a fixed order: dz by warp shuffles and
-// one shared-memory pass per token; dU by per-chunk partial rows summed in
-// reduce.cu.
+// lowrank.py:222-226).  The operands of a tile are staged in shared memory, so U is
+// read once per tile and dy / x once per group of 8 ranks.  All reductions have a
+// fixed order: dz within a block (channel chunks in order, slices in order); dU by
+// per-chunk partial rows summed in reduce.cu.
 #include "common.cuh"
 
 namespace dynconv {
