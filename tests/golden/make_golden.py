@@ -42,6 +42,10 @@ CASES = [
     ("lr_r16_w3_d48_res", "lowrank", dict(B=2, T=13, D=48, R=16, W=3), False, True),
     ("lr_t_lt_w", "lowrank", dict(B=1, T=3, D=16, R=15, W=4), True, True),
     ("lr_r63_w2_static", "lowrank", dict(B=1, T=16, D=16, R=63, W=2), True, False),
+    # taps beyond 4 (the reference pads W to a power of two internally, headwise.py:226)
+    ("hw_hs4_w6_static_res", "headwise", dict(B=2, T=21, D=32, H=8, W=6), True, True),
+    ("lr_r15_w8_static_res", "lowrank", dict(B=2, T=25, D=32, R=15, W=8), True, True),
+    ("lr_r63_w5_static", "lowrank", dict(B=1, T=18, D=16, R=63, W=5), True, False),
 ]
 
 
